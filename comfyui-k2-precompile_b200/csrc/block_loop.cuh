@@ -1,0 +1,119 @@
+// block_loop.cuh -- the native block loop: issues the whole per-block kernel
+// sequence for N transformer blocks on one stream.
+//
+// Replaces the block loop that the reference's Inductor cpp_wrapper entry runs
+// through NativeGraph::run (native_runtime.cpp:543-571) over graph_model.block's
+// input-quant chain (graph_model.py:108-114, 266-295):
+//   norm_quant(x; prenorm, ps, ph)        -> xq, xs
+//   qkv (QK-norm + RoPE on Q and K)       -> q, k, v
+//   attention (+ fused H128/INT4 of o)    -> oq, os
+//   out-proj, gated residual with pg      -> x1 = x + pg * proj
+//   norm_quant(x1; postnorm, ss, sh)      -> xq, xs
+//   gate/up + SwiGLU + INT4 requant       -> hq, hs
+//   down-proj, gated residual with sg     -> x  = x1 + sg * proj
+// Seven launches per block, all on the caller's stream, nothing allocated:
+// the caller passes a workspace of k2b_block_workspace_bytes() bytes.  The
+// sequence is CUDA-graph capturable (no host synchronisation inside).
+
+namespace k2b {
+static inline size_t ws_align(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct BlockWorkspace {
+  uint8_t* xq; __half* xs;
+  __nv_bfloat16 *q, *k, *v;
+  uint8_t* oq; __half* os;
+  __nv_bfloat16* x1;
+  uint8_t* hq; __half* hs;
+  size_t bytes;
+};
+
+static BlockWorkspace carve_workspace(uint8_t* base, long long rows, int hidden, int heads, int kvheads, int mlp) {
+  BlockWorkspace w;
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += ws_align(n);
+    return p;
+  };
+  w.xq = take((size_t)rows * hidden / 2);
+  w.xs = reinterpret_cast<__half*>(take((size_t)rows * (hidden / 128) * 2));
+  w.q = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * heads * 128 * 2));
+  w.k = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * kvheads * 128 * 2));
+  w.v = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * kvheads * 128 * 2));
+  w.oq = take((size_t)rows * heads * 128 / 2);
+  w.os = reinterpret_cast<__half*>(take((size_t)rows * heads * 2));
+  w.x1 = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * hidden * 2));
+  w.hq = take((size_t)rows * mlp / 2);
+  w.hs = reinterpret_cast<__half*>(take((size_t)rows * (mlp / 128) * 2));
+  w.bytes = off;
+  return w;
+}
+}  // namespace k2b
+
+K2B_EXPORT long long k2b_block_workspace_bytes(int rows, int hidden, int heads, int kvheads, int mlp) {
+  if (rows <= 0 || hidden <= 0 || heads <= 0 || kvheads <= 0 || mlp <= 0) return -1;
+  return (long long)k2b::carve_workspace(nullptr, rows, hidden, heads, kvheads, mlp).bytes;
+}
+
+// Pointer slots of one block in `block_ptrs` (K2B_BLOCK_SLOTS per block).
+enum {
+  K2B_SLOT_PRENORM = 0,   // fp32 [hidden], "w+1" form
+  K2B_SLOT_POSTNORM,      // fp32 [hidden]
+  K2B_SLOT_QNORM,         // fp32 [128]
+  K2B_SLOT_KNORM,         // fp32 [128]
+  K2B_SLOT_WQ, K2B_SLOT_SQ,
+  K2B_SLOT_WK, K2B_SLOT_SK,
+  K2B_SLOT_WV, K2B_SLOT_SV,
+  K2B_SLOT_WO, K2B_SLOT_SO,
+  K2B_SLOT_WG, K2B_SLOT_SG,
+  K2B_SLOT_WU, K2B_SLOT_SU,
+  K2B_SLOT_WD, K2B_SLOT_SD,
+  K2B_SLOT_MOD,           // bf16 [6, batch, hidden]: ps, ph, pg, ss, sh, sg
+  K2B_BLOCK_SLOTS
+};
+
+K2B_EXPORT int k2b_block_slots(void) { return K2B_BLOCK_SLOTS; }
+
+K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, const void* freqs,
+                                  void* workspace, long long workspace_bytes, int batch, int length, int hidden,
+                                  int heads, int kvheads, int mlp, float eps, float qk_eps, void* stream) {
+  using namespace k2b;
+  if (!block_ptrs || nblocks <= 0 || !x || !freqs || !workspace || batch <= 0 || length <= 0 ||
+      hidden != heads * 128 || kvheads <= 0 || mlp <= 0)
+    return (int)cudaErrorInvalidValue;
+  const long long rows = (long long)batch * length;
+  if (rows > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
+  BlockWorkspace w = carve_workspace(static_cast<uint8_t*>(workspace), rows, hidden, heads, kvheads, mlp);
+  if ((long long)w.bytes > workspace_bytes) return (int)cudaErrorInvalidValue;
+  const int m = (int)rows;
+  const long long qst = (long long)heads * 128, kst = (long long)kvheads * 128;
+  for (int blk = 0; blk < nblocks; ++blk) {
+    const void* const* P = block_ptrs + (size_t)blk * K2B_BLOCK_SLOTS;
+    const __nv_bfloat16* mod = static_cast<const __nv_bfloat16*>(P[K2B_SLOT_MOD]);
+    const size_t bh = (size_t)batch * hidden;
+    const __nv_bfloat16 *ps = mod, *ph = mod + bh, *pg = mod + 2 * bh, *ss = mod + 3 * bh, *sh = mod + 4 * bh,
+                        *sg = mod + 5 * bh;
+    int rc = k2b_norm_quant(x, P[K2B_SLOT_PRENORM], ps, ph, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+    if (!rc)
+      rc = k2b_qkv(w.xq, w.xs, P[K2B_SLOT_WQ], P[K2B_SLOT_SQ], P[K2B_SLOT_WK], P[K2B_SLOT_SK], P[K2B_SLOT_WV],
+                   P[K2B_SLOT_SV], nullptr, nullptr, P[K2B_SLOT_QNORM], P[K2B_SLOT_KNORM], freqs, w.q, w.k, w.v,
+                   nullptr, m, length, heads * 128, kvheads * 128, hidden, qk_eps, qk_eps, stream);
+    if (!rc)
+      rc = k2b_attention_quant(w.q, w.k, w.v, w.oq, w.os, batch, heads, kvheads, length, length, 128,
+                               (long long)length * qst, 128, qst, (long long)length * kst, 128, kst,
+                               (long long)length * kst, 128, kst, stream);
+    if (!rc)
+      rc = k2b_gated_residual(w.oq, w.os, P[K2B_SLOT_WO], P[K2B_SLOT_SO], pg, x, w.x1, m, length, hidden,
+                              heads * 128, stream);
+    if (!rc)
+      rc = k2b_norm_quant(w.x1, P[K2B_SLOT_POSTNORM], ss, sh, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+    if (!rc)
+      rc = k2b_swiglu_quant(w.xq, w.xs, P[K2B_SLOT_WG], P[K2B_SLOT_SG], P[K2B_SLOT_WU], P[K2B_SLOT_SU], w.hq, w.hs, m,
+                            mlp, hidden, stream);
+    if (!rc)
+      rc = k2b_gated_residual(w.hq, w.hs, P[K2B_SLOT_WD], P[K2B_SLOT_SD], sg, w.x1, x, m, length, hidden, mlp,
+                              stream);
+    if (rc) return rc;
+  }
+  return 0;
+}

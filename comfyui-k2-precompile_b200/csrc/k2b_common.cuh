@@ -1,0 +1,322 @@
+// k2b_common.cuh -- sm_100a building blocks shared by the k2b kernels:
+// bounded mbarrier waits, TMA loads, tcgen05 (TMEM alloc / MMA / commit /
+// ld / st), UMMA shared-memory descriptors, and the exact scalar helpers that
+// the CPU oracle restates bit for bit (bf16/fp16 rounding, exp, quantisation).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace k2b {
+
+// ------------------------------------------------------------------ errors
+// Device-side error word of the library (one per loaded .so).  Kernels never
+// trap: a wait that runs out of time records a code here, raises the CTA's
+// abort flag, and every role of the CTA unwinds to the teardown.
+__device__ int g_error;
+
+enum DeviceError : int {
+  ERR_WAIT_PRODUCER = 1 << 0,
+  ERR_WAIT_MMA = 1 << 1,
+  ERR_WAIT_UNPACK = 1 << 2,
+  ERR_WAIT_EPILOGUE = 1 << 3,
+  ERR_WAIT_SOFTMAX = 1 << 4,
+  ERR_WAIT_LOAD = 1 << 5,
+};
+
+// Upper bound for any single mbarrier wait.  Normal waits are microseconds.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Bound for the teardown wait on copies/MMAs still in flight after an abort.
+constexpr unsigned long long kDrainLimitNs = 200000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_timer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the completion of phase `parity` of `bar`.  Returns false
+// (after raising *abort and recording `code`) if the CTA was aborted or the
+// wait exceeded kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const unsigned long long t0 = global_timer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((i & 15u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_timer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicOr(&g_error, code);
+        return false;
+      }
+    }
+  }
+}
+
+// Teardown-only wait (ignores the abort flag): lets async copies or MMAs that
+// were already issued land before the CTA releases its shared memory / TMEM.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const unsigned long long t0 = global_timer();
+  while (!mbar_try_wait(a, parity)) {
+    if (global_timer() - t0 > kDrainLimitNs) return;
+  }
+}
+
+// --------------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+// Untiled bulk copy global -> shared (addresses and size 16-byte aligned).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ----------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32.
+__device__ __forceinline__ void mma_i8_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, "
+      "p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem], bf16 x bf16 -> fp32.
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, "
+      "p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem], bf16 x bf16 -> fp32.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, "
+      "p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread completes.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld that also "writes" the destination registers of the
+// preceding tcgen05.ld, so no use of them can be scheduled above the wait.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+// 32 lanes x 16 columns of 32-bit: thread i of the warp receives its lane's 16 columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// UMMA shared-memory descriptor for a 128B-swizzled tile (sm_100 version 1).
+// K-major: rows of 128 B, 8-row atoms 1024 B apart (SBO), LBO unused (1).
+// MN-major: 128 B of MN per K row, 8 K rows per atom (SBO between K atoms),
+// LBO between 64-element MN blocks.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: c_fmt {0:f16,1:f32,2:s32}, a/b fmt {i8: 0 u8 / 1 s8;
+// f16-kind: 0 f16 / 1 bf16}, majors {0:K, 1:MN}.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt, uint32_t a_major,
+                                                  uint32_t b_major, uint32_t m, uint32_t n) {
+  return (c_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | (a_major << 15) | (b_major << 16) | ((n >> 3) << 17) |
+         ((m >> 4) << 24);
+}
+
+// ------------------------------------------------------- packed fp32 math
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, "
+      "%7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ------------------------------------------------- exact scalar contract
+
+// In-register Sylvester H128 on 128 fp32 values: stages h = 1, 2, ..., 64 in
+// that order, (a, b) -> (a + b, a - b) (oracle: k2o_hadamard128 before its
+// final scaling).  Counted stage loop so every index is a compile-time constant.
+__device__ __forceinline__ void hadamard128_regs(float (&v)[128]) {
+#pragma unroll
+  for (int lh = 0; lh < 7; ++lh) {
+    const int h = 1 << lh;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int lo = ((i >> lh) << (lh + 1)) | (i & (h - 1));
+      const float a = v[lo], b = v[lo + h];
+      v[lo] = __fadd_rn(a, b);
+      v[lo + h] = __fsub_rn(a, b);
+    }
+  }
+}
+// These helpers are restated bit for bit by oracle/k2_oracle.c.
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// fp32(1/sqrt(128)), the normalisation of the Sylvester H128 block.
+constexpr float kHadamardScale = 0.0883883461356163024902343750f;
+
+// exp(x): Cody-Waite reduction with a two-part ln2, degree-7 Taylor
+// polynomial in Horner form, exponent-field scaling (oracle: k2o_exp).
+__device__ __forceinline__ float exp_contract(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x < -103.972084045410156f) return 0.0f;
+  float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(n, -0.693145751953125f, x);
+  r = __fmaf_rn(n, -1.428606765330187045037746429443359375e-06f, r);
+  float p = 1.98412698412698412526e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888888894189e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333321769e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666666643537e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666666657415e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int e = (int)n;
+  if (e > 127) {
+    p = __fmul_rn(p, 1.7014118346046923e38f);
+    e -= 127;
+  }
+  if (e < -126) {
+    p = __fmul_rn(p, 1.1754943508222875e-38f);
+    e += 126;
+  }
+  return __fmul_rn(p, __int_as_float((e + 127) << 23));
+}
+__device__ __forceinline__ float silu_contract(float x) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, exp_contract(-x)));
+}
+__device__ __forceinline__ float sigmoid_contract(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_contract(-x)));
+}
+
+// INT4 code of v for the dequant scale sd > 0: clamp(rint(v / sd), -8, 7)
+// with a correctly rounded division.  The product with the reciprocal picks
+// the same integer unless v/sd lies within ~1e-6 of a half-integer, where the
+// exact division decides.
+__device__ __forceinline__ int quant_code(float v, float sd, float rcp) {
+  float t = __fmul_rn(v, rcp);
+  float r = rintf(t);
+  if (fabsf(fabsf(__fsub_rn(t, r)) - 0.5f) < 1.0e-3f) r = rintf(__fdiv_rn(v, sd));
+  r = fminf(fmaxf(r, -8.0f), 7.0f);
+  return (int)r;
+}
+// fp16 scale of a group with absolute maximum amax: fp16(min(amax/7, 65504)).
+__device__ __forceinline__ __half group_scale(float amax) {
+  float sf = __fdiv_rn(amax, 7.0f);
+  sf = fminf(sf, 65504.0f);
+  return __float2half_rn(sf);
+}
+
+}  // namespace k2b

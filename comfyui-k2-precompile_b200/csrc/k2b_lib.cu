@@ -1,0 +1,376 @@
+// k2b_lib.cu -- the single translation unit of libk2b: kernels + C-ABI.
+//
+// Every exported entry point takes plain device pointers, sizes and a
+// cudaStream_t (as void*), launches on that stream, allocates nothing, and
+// returns 0 or a cudaError_t code (cudaErrorInvalidValue for shapes/pointers
+// the kernels do not support).  Declarations: include/k2b.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/k2b.h"
+#include "attention.cuh"
+#include "gemm_w4a4.cuh"
+#include "k2b_common.cuh"
+#include "norm_quant.cuh"
+
+#define K2B_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace k2b {
+
+// ------------------------------------------------------------- utilities
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D row-major tensor map: `cols` elements per row (innermost), `rows` rows.
+static int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, size_t esize, const void* base, uint64_t cols,
+                       uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows,
+                       CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return (int)cudaErrorInitializationError;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  (void)esize;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+// 4-D map (d, token, head, batch) over a strided bf16 [B, H, L, D] view.
+static int make_map_4d_bf16(CUtensorMap* map, const void* base, uint64_t D, uint64_t L, uint64_t H, uint64_t B,
+                            uint64_t s_tok, uint64_t s_head, uint64_t s_batch, uint32_t box_d, uint32_t box_tok) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return (int)cudaErrorInitializationError;
+  cuuint64_t dims[4] = {D, L, H, B};
+  cuuint64_t strides[3] = {s_tok * 2, s_head * 2, s_batch * 2};
+  cuuint32_t box[4] = {box_d, box_tok, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+static int launch_status() { return (int)cudaGetLastError(); }
+
+// ----------------------------------------------------------- norm_quant
+template <bool NORM>
+static int norm_quant_launch(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
+                             int rows, int K, int length, int cut, int batch, float eps, cudaStream_t st) {
+  if (rows <= 0 || K <= 0 || K % 512 || (NORM && (length <= 0 || batch <= 0))) return (int)cudaErrorInvalidValue;
+  if (!aligned16(x) || !aligned16(q) || (NORM && (!aligned16(w) || !aligned16(scale) || !aligned16(shift))))
+    return (int)cudaErrorInvalidValue;
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wf = static_cast<const float*>(w);
+  const auto* sc = static_cast<const __nv_bfloat16*>(scale);
+  const auto* sh = static_cast<const __nv_bfloat16*>(shift);
+  auto* qo = static_cast<uint8_t*>(q);
+  auto* so = static_cast<__half*>(s);
+  switch (K / 512) {
+#define K2B_NQ_CASE(S)                                                                                \
+  case S:                                                                                             \
+    norm_quant_kernel<S, NORM><<<rows, 128, 0, st>>>(xb, wf, sc, sh, qo, so, length, cut, batch, eps); \
+    break;
+    K2B_NQ_CASE(1)
+    K2B_NQ_CASE(2)
+    K2B_NQ_CASE(4)
+    K2B_NQ_CASE(8)
+    K2B_NQ_CASE(12)
+    K2B_NQ_CASE(16)
+    K2B_NQ_CASE(24)
+    K2B_NQ_CASE(32)
+#undef K2B_NQ_CASE
+    default:
+      return (int)cudaErrorInvalidValue;
+  }
+  return launch_status();
+}
+
+// --------------------------------------------------- weight preparation
+// Packed INT4 [n, k/2] + fp16 group scales [n, k/128] -> s8 [.., k] holding
+// 16*code (same nibble placement as the in-kernel A unpacker) at row
+// dst(r) = (r / block_rows) * dst_block_stride + dst_offset + r % block_rows,
+// and fp32 scales transposed to [k/128, scale_ld] at column dst(r).
+__global__ void prepare_weight_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ ws,
+                                      int8_t* __restrict__ out, float* __restrict__ st, int n, int k, int block_rows,
+                                      int dst_block_stride, int dst_offset, int scale_ld) {
+  const int chunks = k / 32;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)n * chunks) return;
+  const int r = (int)(idx / chunks), c = (int)(idx % chunks);
+  const int64_t dr = (int64_t)(r / block_rows) * dst_block_stride + dst_offset + (r % block_rows);
+  const uint4 v = *reinterpret_cast<const uint4*>(wp + (int64_t)r * (k / 2) + 16 * c);
+  uint4 lo, hi;
+  unpack_chunk(v, lo, hi);
+  *reinterpret_cast<uint4*>(out + dr * k + 32 * c) = lo;
+  *reinterpret_cast<uint4*>(out + dr * k + 32 * c + 16) = hi;
+  if ((c & 3) == 0) st[(int64_t)(c >> 2) * scale_ld + dr] = __half2float(ws[(int64_t)r * (k / 128) + (c >> 2)]);
+}
+
+// ---------------------------------------------------------------- GEMM
+struct SegDesc {
+  int kind;
+  int n;                  // columns (= weight rows) of this segment
+  const void* w;          // prepared s8 [n, K]
+  const void* wscale;     // fp32 [K/128, n]
+  void* out;
+  int ld;
+  const float* normw;
+  float eps;
+  void* out_scale;
+  const void* w2;         // SwiGLU: up projection, prepared s8 [n, K]
+  const void* wscale2;    // SwiGLU: fp32 [K/128, n]
+};
+
+static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDesc* segs, int nseg, int length,
+                       const float* freqs, const void* gate, const void* resid, cudaStream_t st) {
+  if (M <= 0 || K <= 0 || K % 128 || nseg < 1 || nseg > 4 || length <= 0) return (int)cudaErrorInvalidValue;
+  if (!aligned16(a) || !sa) return (int)cudaErrorInvalidValue;
+  CUtensorMap amap;
+  WeightMaps wm;
+  memset(&wm, 0, sizeof(wm));
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  int tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const SegDesc& d = segs[i];
+    const bool pairw = d.kind == SEG_SWIGLU || d.kind == SEG_SWIGLU_BF16;
+    if (pairw && nseg != 1) return (int)cudaErrorInvalidValue;
+    const int tile_n = pairw ? GEMM_BN / 2 : GEMM_BN;
+    if (d.n <= 0 || d.n % tile_n || !aligned16(d.w) || !aligned16(d.wscale) || !d.out) return (int)cudaErrorInvalidValue;
+    int rc = make_map_2d(&wm.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w, (uint64_t)K, (uint64_t)d.n, (uint64_t)K,
+                         128, tile_n, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (pairw) {
+      if (!aligned16(d.w2) || !aligned16(d.wscale2)) return (int)cudaErrorInvalidValue;
+      rc = make_map_2d(&wm.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w2, (uint64_t)K, (uint64_t)d.n, (uint64_t)K, 128,
+                       tile_n, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
+    GemmSegment& g = p.seg[i];
+    g.tiles = d.n / tile_n;
+    g.kind = d.kind;
+    g.n = d.n;
+    g.ld = d.ld;
+    g.out = d.out;
+    g.wscale = static_cast<const float*>(d.wscale);
+    g.wscale2 = static_cast<const float*>(d.wscale2);
+    g.normw = d.normw;
+    g.eps = d.eps;
+    g.out_scale = static_cast<__half*>(d.out_scale);
+    if (d.kind == SEG_QKNORM && (!d.normw || !freqs || !aligned16(freqs))) return (int)cudaErrorInvalidValue;
+    if (d.kind == SEG_RESIDUAL && (!gate || !resid || !aligned16(gate) || !aligned16(resid) || d.ld % 8))
+      return (int)cudaErrorInvalidValue;
+    if (d.kind == SEG_SWIGLU && (!d.out_scale || d.ld % 16 || !aligned16(d.out))) return (int)cudaErrorInvalidValue;
+    if ((d.kind == SEG_BF16 || d.kind == SEG_SIGMOID || d.kind == SEG_QKNORM || d.kind == SEG_SWIGLU_BF16) &&
+        (d.ld % 8 || !aligned16(d.out)))
+      return (int)cudaErrorInvalidValue;
+    if (d.kind == SEG_F32 && (d.ld % 4 || !aligned16(d.out))) return (int)cudaErrorInvalidValue;
+    tiles += g.tiles;
+  }
+  int rc = make_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, (uint64_t)K / 2, (uint64_t)M, (uint64_t)K / 2, 64,
+                       GEMM_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  p.nseg = nseg;
+  p.M = M;
+  p.K = K;
+  p.G = K / 128;
+  p.length = length;
+  p.sa = static_cast<const __half*>(sa);
+  p.freqs = freqs;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.resid = static_cast<const __nv_bfloat16*>(resid);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_w4a4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    attr_set[dev] = true;
+  }
+  dim3 grid((M + GEMM_BM - 1) / GEMM_BM, tiles);
+  gemm_w4a4_kernel<<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(amap, wm, p);
+  return launch_status();
+}
+
+// ----------------------------------------------------------- attention
+static int attention_launch(const void* q, const void* k, const void* v, const void* gate, void* out, void* oq,
+                            void* os, int batch, int heads, int kvheads, int lq, int lk, int dim, long long q_sb,
+                            long long q_sh, long long q_st, long long k_sb, long long k_sh, long long k_st,
+                            long long v_sb, long long v_sh, long long v_st, int gate_kind, cudaStream_t st) {
+  if (batch <= 0 || heads <= 0 || kvheads <= 0 || heads % kvheads || (heads / kvheads) % 2 || lq <= 0 || lk <= 0 ||
+      dim != FA_D)
+    return (int)cudaErrorInvalidValue;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (!out && !oq) || (oq && !os)) return (int)cudaErrorInvalidValue;
+  if (out && !aligned16(out)) return (int)cudaErrorInvalidValue;
+  if (oq && !aligned16(oq)) return (int)cudaErrorInvalidValue;
+  if (gate && (!aligned16(gate) || (gate_kind != 1 && gate_kind != 2))) return (int)cudaErrorInvalidValue;
+  // TMA strides must be multiples of 16 bytes (8 bf16 elements)
+  const long long strides[9] = {q_sb, q_sh, q_st, k_sb, k_sh, k_st, v_sb, v_sh, v_st};
+  for (long long s : strides)
+    if (s <= 0 || s % 8) return (int)cudaErrorInvalidValue;
+  AttnMaps maps;
+  int rc = make_map_4d_bf16(&maps.q, q, FA_D, lq, heads, batch, q_st, q_sh, q_sb, 64, FA_BM);
+  if (!rc) rc = make_map_4d_bf16(&maps.k, k, FA_D, lk, kvheads, batch, k_st, k_sh, k_sb, 64, FA_BN);
+  if (!rc) rc = make_map_4d_bf16(&maps.v, v, FA_D, lk, kvheads, batch, v_st, v_sh, v_sb, 64, FA_BN);
+  if (rc) return rc;
+  AttnParams p;
+  p.batch = batch;
+  p.heads = heads;
+  p.kvheads = kvheads;
+  p.lq = lq;
+  p.lk = lk;
+  p.c = (float)(1.4426950408889634 / 11.313708498984761);  // log2(e)/sqrt(128)
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.gate_kind = gate ? gate_kind : 0;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.oq = static_cast<uint8_t*>(oq);
+  p.os = static_cast<__half*>(os);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    attr_set[dev] = true;
+  }
+  dim3 grid((lq + FA_BM - 1) / FA_BM, heads / 2, batch);
+  attention_kernel<<<grid, FA_THREADS, FA_SMEM_BYTES, st>>>(maps, p);
+  return launch_status();
+}
+
+}  // namespace k2b
+
+using namespace k2b;
+
+// =====================================================================
+//                                C-ABI
+// =====================================================================
+
+K2B_EXPORT const char* k2b_version(void) { return "k2b 0.1 sm_100a"; }
+
+K2B_EXPORT int k2b_device_error(int reset, void* stream) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_error, sizeof(int), 0, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (e != cudaSuccess) return -(int)e;
+  e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return -(int)e;
+  if (reset) {
+    int z = 0;
+    e = cudaMemcpyToSymbolAsync(g_error, &z, sizeof(int), 0, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return -(int)e;
+  }
+  return v;
+}
+
+K2B_EXPORT int k2b_norm_quant(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
+                              int rows, int K, int length, int cut, int batch, float eps, void* stream) {
+  return norm_quant_launch<true>(x, w, scale, shift, q, s, rows, K, length, cut, batch, eps, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_rotate_quant(const void* x, void* q, void* s, int rows, int K, void* stream) {
+  return norm_quant_launch<false>(x, nullptr, nullptr, nullptr, q, s, rows, K, 1, -1, 1, 0.0f, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_prepare_weight(const void* w_packed, const void* w_scale, void* w_prepared, void* scale_t, int n,
+                                  int k, int block_rows, int dst_block_stride, int dst_offset, int scale_ld,
+                                  void* stream) {
+  if (n <= 0 || k <= 0 || k % 128 || block_rows <= 0 || dst_block_stride < block_rows || dst_offset < 0 ||
+      scale_ld <= 0 || !aligned16(w_packed) || !aligned16(w_prepared))
+    return (int)cudaErrorInvalidValue;
+  const int64_t total = (int64_t)n * (k / 32);
+  const int threads = 256;
+  prepare_weight_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint8_t*>(w_packed), static_cast<const __half*>(w_scale), static_cast<int8_t*>(w_prepared),
+      static_cast<float*>(scale_t), n, k, block_rows, dst_block_stride, dst_offset, scale_ld);
+  return launch_status();
+}
+
+K2B_EXPORT int k2b_gemm_f32(const void* a, const void* sa, const void* w, const void* wscale, void* out, int m, int n,
+                            int k, void* stream) {
+  SegDesc d = {SEG_F32, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_gemm_bf16(const void* a, const void* sa, const void* w, const void* wscale, void* out, int m, int n,
+                             int k, void* stream) {
+  SegDesc d = {SEG_BF16, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_qkv(const void* a, const void* sa, const void* wq, const void* swq, const void* wk,
+                       const void* swk, const void* wv, const void* swv, const void* wg, const void* swg,
+                       const void* nq, const void* nk, const void* freqs, void* qo, void* ko, void* vo, void* go,
+                       int m, int length, int qwidth, int kvwidth, int k, float eq, float ek, void* stream) {
+  if (qwidth % 256 || kvwidth % 256) return (int)cudaErrorInvalidValue;
+  SegDesc d[4] = {
+      {SEG_QKNORM, qwidth, wq, swq, qo, qwidth, static_cast<const float*>(nq), eq, nullptr, nullptr, nullptr},
+      {SEG_QKNORM, kvwidth, wk, swk, ko, kvwidth, static_cast<const float*>(nk), ek, nullptr, nullptr, nullptr},
+      {SEG_BF16, kvwidth, wv, swv, vo, kvwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+      {SEG_SIGMOID, qwidth, wg, swg, go, qwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+  };
+  const int nseg = (wg && go) ? 4 : 3;
+  return gemm_launch(a, sa, m, k, d, nseg, length, static_cast<const float*>(freqs), nullptr, nullptr,
+                     (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_gated_residual(const void* a, const void* sa, const void* w, const void* wscale, const void* gate,
+                                  const void* residual, void* out, int m, int length, int n, int k, void* stream) {
+  SegDesc d = {SEG_RESIDUAL, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a, sa, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_swiglu_quant(const void* a, const void* sa, const void* wg, const void* sg, const void* wu,
+                                const void* su, void* hq, void* hs, int m, int width, int k, void* stream) {
+  if (width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU, width, wg, sg, hq, width / 2, nullptr, 0.0f, hs, wu, su};
+  return gemm_launch(a, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_swiglu_bf16(const void* a, const void* sa, const void* wg, const void* sg, const void* wu,
+                               const void* su, void* h, int m, int width, int k, void* stream) {
+  if (width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU_BF16, width, wg, sg, h, width, nullptr, 0.0f, nullptr, wu, su};
+  return gemm_launch(a, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_attention(const void* q, const void* k, const void* v, const void* gate, void* out, int batch,
+                             int heads, int kvheads, int lq, int lk, int dim, long long q_sb, long long q_sh,
+                             long long q_st, long long k_sb, long long k_sh, long long k_st, long long v_sb,
+                             long long v_sh, long long v_st, int gate_kind, void* stream) {
+  return attention_launch(q, k, v, gate, out, nullptr, nullptr, batch, heads, kvheads, lq, lk, dim, q_sb, q_sh, q_st,
+                          k_sb, k_sh, k_st, v_sb, v_sh, v_st, gate_kind, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_attention_quant(const void* q, const void* k, const void* v, void* oq, void* os, int batch,
+                                   int heads, int kvheads, int lq, int lk, int dim, long long q_sb, long long q_sh,
+                                   long long q_st, long long k_sb, long long k_sh, long long k_st, long long v_sb,
+                                   long long v_sh, long long v_st, void* stream) {
+  return attention_launch(q, k, v, nullptr, nullptr, oq, os, batch, heads, kvheads, lq, lk, dim, q_sb, q_sh, q_st,
+                          k_sb, k_sh, k_st, v_sb, v_sh, v_st, 0, (cudaStream_t)stream);
+}
+
+#include "abi_reference.cuh"
+#include "block_loop.cuh"

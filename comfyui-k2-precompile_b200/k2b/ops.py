@@ -1,0 +1,267 @@
+"""Torch-level wrappers over the libk2b C ABI.
+
+Each op validates devices, dtypes, shapes and contiguity the way the reference's
+C++ side does before it dlsym-calls a kernel (TORCH_CHECK-style errors,
+native_runtime.cpp:262-271, 399-423), allocates outputs with torch.empty
+(the kernels never allocate), launches on torch's current CUDA stream, and
+raises ``K2BError`` on a non-zero status.  Nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from ._native import K2BError, check, lib
+
+GROUP = 128
+HEAD_DIM = 128
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(*ts: Optional[torch.Tensor]) -> None:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        _need(t.is_cuda, "k2b ops need CUDA tensors")
+        _need(t.is_contiguous(), "k2b ops need contiguous tensors")
+        dev = t.device if dev is None else dev
+        _need(t.device == dev, "k2b op inputs must share one device")
+
+
+# ------------------------------------------------------------------ weights
+
+@dataclass
+class PreparedWeight:
+    """Device-resident INT4 weight in the GEMM's streaming layout."""
+
+    w: torch.Tensor      # int8 [n, k] (16 x code, nibble-interleaved per 32 columns)
+    scale: torch.Tensor  # fp32 [k/128, n]
+
+    @property
+    def n(self) -> int:
+        return int(self.w.shape[0])
+
+    @property
+    def k(self) -> int:
+        return int(self.w.shape[1])
+
+
+def prepare_weight(packed: torch.Tensor, scales: torch.Tensor) -> PreparedWeight:
+    """Packed INT4 [n, k/2] (uint8) + fp16 group scales [n, k/128] ->
+    PreparedWeight.  Registration-time step (weights stay resident)."""
+    _cuda(packed, scales)
+    _need(packed.dtype == torch.uint8 and scales.dtype == torch.float16, "packed u8 + fp16 scales expected")
+    n, k2 = packed.shape
+    k = 2 * k2
+    _need(k % GROUP == 0 and tuple(scales.shape) == (n, k // GROUP), "weight scale shape mismatch")
+    w = torch.empty((n, k), dtype=torch.int8, device=packed.device)
+    s = torch.empty((k // GROUP, n), dtype=torch.float32, device=packed.device)
+    check(lib().k2b_prepare_weight(_p(packed), _p(scales), _p(w), _p(s), n, k, n, n, 0, n, _stream()),
+          "k2b_prepare_weight")
+    return PreparedWeight(w, s)
+
+
+# --------------------------------------------------------------- norm_quant
+
+def norm_quant(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, *,
+               length: Optional[int] = None, cut: int = -1, eps: float = 1e-6
+               ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Fused RMSNorm + adaLN + H128 + group-128 INT4 (k2_native::norm_quant).
+
+    x bf16 [..., K] (rows = prod of leading dims; ``length`` rows per latent,
+    default = x.shape[-2] for 3-D x else all rows); w fp32 [K] in the "w+1"
+    form; scale/shift bf16 [nb, K] (any shape ending in K).
+    Returns (q uint8 [rows, K/2], s fp16 [rows, K/128])."""
+    _cuda(x, w, scale, shift)
+    _need(x.dtype == torch.bfloat16 and scale.dtype == torch.bfloat16 and shift.dtype == torch.bfloat16,
+          "norm_quant: bf16 activations and modulation expected")
+    _need(w.dtype == torch.float32, "norm_quant: fp32 norm weight expected")
+    K = int(x.shape[-1])
+    rows = x.numel() // K
+    if length is None:
+        length = int(x.shape[-2]) if x.dim() == 3 else rows
+    batch = max(1, rows // length)
+    _need(w.numel() == K and scale.shape[-1] == K and shift.shape[-1] == K, "norm_quant: width mismatch")
+    nb = scale.numel() // K
+    _need(nb >= (2 * batch if cut >= 0 else batch) and shift.numel() == scale.numel(),
+          "norm_quant: modulation rows do not cover the batch")
+    q = torch.empty((rows, K // 2), dtype=torch.uint8, device=x.device)
+    s = torch.empty((rows, K // GROUP), dtype=torch.float16, device=x.device)
+    check(lib().k2b_norm_quant(_p(x), _p(w), _p(scale), _p(shift), _p(q), _p(s), rows, K, length, cut, batch,
+                               ctypes.c_float(eps), _stream()), "k2b_norm_quant")
+    return q, s
+
+
+def rotate_quant(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [..., K] -> (uint8 [rows, K/2], fp16 [rows, K/128])."""
+    _cuda(x)
+    _need(x.dtype == torch.bfloat16, "rotate_quant: bf16 expected")
+    K = int(x.shape[-1])
+    rows = x.numel() // K
+    q = torch.empty((rows, K // 2), dtype=torch.uint8, device=x.device)
+    s = torch.empty((rows, K // GROUP), dtype=torch.float16, device=x.device)
+    check(lib().k2b_rotate_quant(_p(x), _p(q), _p(s), rows, K, _stream()), "k2b_rotate_quant")
+    return q, s
+
+
+# --------------------------------------------------------------------- GEMM
+
+def _act(a: torch.Tensor, sa: torch.Tensor, k: int) -> int:
+    _need(a.dtype == torch.uint8 and sa.dtype == torch.float16, "packed uint8 activations + fp16 scales expected")
+    _need(a.dim() == 2 and a.shape[1] * 2 == k and tuple(sa.shape) == (a.shape[0], k // GROUP),
+          "activation / weight K mismatch")
+    return int(a.shape[0])
+
+
+def gemm_f32(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Tensor:
+    _cuda(a, sa, W.w, W.scale)
+    m = _act(a, sa, W.k)
+    out = torch.empty((m, W.n), dtype=torch.float32, device=a.device)
+    check(lib().k2b_gemm_f32(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
+          "k2b_gemm_f32")
+    return out
+
+
+def gemm_bf16(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Tensor:
+    _cuda(a, sa, W.w, W.scale)
+    m = _act(a, sa, W.k)
+    out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
+    check(lib().k2b_gemm_bf16(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
+          "k2b_gemm_bf16")
+    return out
+
+
+def qkv(a: torch.Tensor, sa: torch.Tensor, wq: PreparedWeight, wk: PreparedWeight, wv: PreparedWeight,
+        nq: torch.Tensor, nk: torch.Tensor, freqs: torch.Tensor, *, length: int, eps_q: float = 1e-6,
+        eps_k: float = 1e-6, wg: Optional[PreparedWeight] = None):
+    """Fused Q/K/V(/gate) projection with QK RMSNorm + RoPE (k2_native::qkv_prepared).
+
+    Returns token-major bf16 (q [m, Hq*128], k [m, Hkv*128], v [m, Hkv*128],
+    gate [m, Hq*128] or None)."""
+    _cuda(a, sa, wq.w, wk.w, wv.w, nq, nk, freqs, None if wg is None else wg.w)
+    m = _act(a, sa, wq.k)
+    _need(wk.k == wq.k and wv.k == wq.k and wk.n == wv.n, "qkv weight shapes")
+    _need(nq.dtype == torch.float32 and nk.dtype == torch.float32 and nq.numel() == HEAD_DIM and
+          nk.numel() == HEAD_DIM, "qkv: fp32 [128] q/k norm weights expected")
+    _need(freqs.dtype == torch.float32 and freqs.numel() == length * 64 * 4, "qkv: freqs fp32 [length,64,2,2]")
+    _need(m % length == 0, "qkv: rows must be a whole number of latents")
+    qo = torch.empty((m, wq.n), dtype=torch.bfloat16, device=a.device)
+    ko = torch.empty((m, wk.n), dtype=torch.bfloat16, device=a.device)
+    vo = torch.empty((m, wv.n), dtype=torch.bfloat16, device=a.device)
+    go = None
+    if wg is not None:
+        _need(wg.n == wq.n and wg.k == wq.k, "qkv gate weight shape")
+        go = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
+    check(lib().k2b_qkv(_p(a), _p(sa), _p(wq.w), _p(wq.scale), _p(wk.w), _p(wk.scale), _p(wv.w), _p(wv.scale),
+                        _p(None if wg is None else wg.w), _p(None if wg is None else wg.scale), _p(nq), _p(nk),
+                        _p(freqs), _p(qo), _p(ko), _p(vo), _p(go), m, length, wq.n, wk.n, wq.k,
+                        ctypes.c_float(eps_q), ctypes.c_float(eps_k), _stream()), "k2b_qkv")
+    return qo, ko, vo, go
+
+
+def gated_residual(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, gate: torch.Tensor,
+                   residual: torch.Tensor, *, length: int) -> torch.Tensor:
+    """out = bf16(residual + bf16(bf16(a@W) * gate[row // length]))."""
+    _cuda(a, sa, W.w, gate, residual)
+    m = _act(a, sa, W.k)
+    _need(gate.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16, "gated_residual: bf16 expected")
+    _need(residual.numel() == m * W.n and gate.numel() == (m // length) * W.n and m % length == 0,
+          "gated_residual: shapes")
+    out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
+    check(lib().k2b_gated_residual(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(gate), _p(residual), _p(out), m, length,
+                                   W.n, W.k, _stream()), "k2b_gated_residual")
+    return out
+
+
+def swiglu_quant(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: PreparedWeight):
+    """Gate/up + SwiGLU + H128 + INT4 -> (hq uint8 [m, F/2], hs fp16 [m, F/128])."""
+    _cuda(a, sa, wg.w, wu.w)
+    m = _act(a, sa, wg.k)
+    _need(wu.n == wg.n and wu.k == wg.k, "swiglu weight shapes")
+    F = wg.n
+    hq = torch.empty((m, F // 2), dtype=torch.uint8, device=a.device)
+    hs = torch.empty((m, F // GROUP), dtype=torch.float16, device=a.device)
+    check(lib().k2b_swiglu_quant(_p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(hq), _p(hs), m,
+                                 F, wg.k, _stream()), "k2b_swiglu_quant")
+    return hq, hs
+
+
+def swiglu_bf16(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: PreparedWeight) -> torch.Tensor:
+    _cuda(a, sa, wg.w, wu.w)
+    m = _act(a, sa, wg.k)
+    _need(wu.n == wg.n and wu.k == wg.k, "swiglu weight shapes")
+    h = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
+    check(lib().k2b_swiglu_bf16(_p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(h), m, wg.n,
+                                wg.k, _stream()), "k2b_swiglu_bf16")
+    return h
+
+
+# ---------------------------------------------------------------- attention
+
+def _bhld(t: torch.Tensor, name: str):
+    _need(t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 4, f"{name}: bf16 [B,H,L,D] CUDA tensor expected")
+    _need(t.shape[-1] == HEAD_DIM and t.stride(-1) == 1, f"{name}: head dim 128, contiguous last dim")
+    return int(t.stride(0)), int(t.stride(1)), int(t.stride(2))
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: Optional[torch.Tensor] = None,
+              gate: Optional[torch.Tensor] = None, gate_is_sigmoid: bool = True) -> torch.Tensor:
+    """GQA flash attention with the Kohaku FA contract
+    (KohakuKernelRouter/attention.py:146-193): q [B,Hq,L,D], k/v [B,Hkv,Lk,D]
+    (any strides with a contiguous last dim) -> out [B, L, Hq*D]."""
+    _need(mask is None, "k2b attention: attention masks are not supported on the B200 path")
+    qs, ks, vs = _bhld(q, "q"), _bhld(k, "k"), _bhld(v, "v")
+    B, H, L, D = q.shape
+    _need(k.shape[0] == B and k.shape[:3] == v.shape[:3] and H % k.shape[1] == 0, "attention: GQA shapes")
+    _need(q.device == k.device == v.device, "attention: one device")
+    out = torch.empty((B, L, H * D), dtype=q.dtype, device=q.device)
+    if L == 0:
+        return out
+    gate_kind = 0
+    if gate is not None:
+        _need(tuple(gate.shape) == tuple(out.shape) and gate.dtype == q.dtype and gate.device == q.device,
+              "attention: gate must match the output")
+        gate = gate.contiguous()
+        gate_kind = 2 if gate_is_sigmoid else 1
+    check(lib().k2b_attention(_p(q), _p(k), _p(v), _p(gate), _p(out), B, H, int(k.shape[1]), L, int(k.shape[2]), D,
+                              *qs, *ks, *vs, gate_kind, _stream()), "k2b_attention")
+    return out
+
+
+def attention_quant(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    """Attention whose output is stored H128-rotated and INT4-quantised:
+    (oq uint8 [B*L, Hq*64], os fp16 [B*L, Hq])."""
+    qs, ks, vs = _bhld(q, "q"), _bhld(k, "k"), _bhld(v, "v")
+    B, H, L, D = q.shape
+    _need(k.shape[0] == B and k.shape[:3] == v.shape[:3] and H % k.shape[1] == 0, "attention: GQA shapes")
+    oq = torch.empty((B * L, H * D // 2), dtype=torch.uint8, device=q.device)
+    os_ = torch.empty((B * L, H), dtype=torch.float16, device=q.device)
+    check(lib().k2b_attention_quant(_p(q), _p(k), _p(v), _p(oq), _p(os_), B, H, int(k.shape[1]), L,
+                                    int(k.shape[2]), D, *qs, *ks, *vs, _stream()), "k2b_attention_quant")
+    return oq, os_
+
+
+def device_error(reset: bool = True) -> int:
+    return int(lib().k2b_device_error(1 if reset else 0, _stream()))
+
+
+__all__ = [
+    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "rotate_quant", "gemm_f32", "gemm_bf16", "qkv",
+    "gated_residual", "swiglu_quant", "swiglu_bf16", "attention", "attention_quant", "device_error",
+]

@@ -1,0 +1,173 @@
+/*
+ * k2b.h -- C ABI of libk2b, the B200 (sm_100a) kernel library for the Krea2
+ * W4A4 DiT block hot path.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers, sizes, and a cudaStream_t passed as void*; every
+ *     launch goes on that stream (the reference launches on the caller's
+ *     current stream, native_runtime.cpp:195);
+ *   - nothing is allocated: the caller owns every output and workspace
+ *     (native_runtime.cpp:373,413-414,441);
+ *   - return 0 on success, otherwise a cudaError_t value; 1
+ *     (cudaErrorInvalidValue) for unsupported shapes, dtypes or misaligned
+ *     pointers, as kernels/norm_quant.cu:92 does;
+ *   - kernels never trap; a device-side wait that runs out of time records a
+ *     bit readable through k2b_device_error().
+ *
+ * Data contract (BASELINE contract; the reference's per-row fp32 scales are
+ * replaced by group-128 fp16 scales):
+ *   - activations: bf16 row-major [rows, K];
+ *   - packed INT4: uint8 [rows, K/2], two codes per byte, low nibble = even
+ *     column, plus fp16 scales [rows, K/128]; codes are clamp(rne(v/s),-8,7) of
+ *     the Sylvester H128-rotated values, s = fp16(absmax/7);
+ *   - prepared weights (k2b_prepare_weight): int8 [n, K] and fp32 scales
+ *     [K/128, n]; GEMM dequant: p = sum_g fmaf(fp32(acc_g*sA[r,g]), sW[c,g], .)
+ *     in increasing g;
+ *   - RMSNorm weights are fp32 in the "w+1" form (native_schedule.py:252-253).
+ */
+#ifndef K2B_H
+#define K2B_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library identification string. */
+const char* k2b_version(void);
+
+/* Reads (and with reset != 0 clears) the device-side error word: bit 0..5 =
+ * a bounded wait in the TMA / MMA / unpack / epilogue / softmax / load role
+ * gave up.  Synchronises `stream`.  Returns the word, or -cudaError. */
+int k2b_device_error(int reset, void* stream);
+
+/* ----------------------------------------------------------- norm_quant --
+ * Fused RMSNorm -> adaLN modulation -> H128 rotation -> group-128 INT4.
+ * Replaces k2_norm_mod_quant4 (kernels/norm_quant.cu:89-91) behind the op
+ * k2_native::norm_quant (native_runtime.cpp:432-447).
+ *   y = bf16((x*inv)*(w+1)), y = bf16(y*bf16(scale+1)), v = bf16(y+shift),
+ *   inv = rsqrt_rn(sum(x^2)/K + eps) in the reference's reduction order;
+ * the modulation row is b = row/length (+batch when cut >= 0 and
+ * row%length >= cut), kernels/norm_quant.cu:32.
+ * x bf16 [rows,K]; w fp32 [K]; scale/shift bf16 [nb,K]; q u8 [rows,K/2];
+ * s fp16 [rows,K/128].  K must be one of 512*{1,2,4,8,12,16,24,32}. */
+int k2b_norm_quant(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
+                   int rows, int K, int length, int cut, int batch, float eps, void* stream);
+
+/* H128 rotation + group-128 INT4 of a bf16 activation: the input quantisation
+ * `quantize()` performs before an INT4 projection (native_runtime.cpp:268-271;
+ * comfy-kitchen quantize_int4_rowwise_convrot64 via k2_quant4,
+ * kernels/native_dispatch.cu:23-25).  Same K constraint as k2b_norm_quant. */
+int k2b_rotate_quant(const void* x, void* q, void* s, int rows, int K, void* stream);
+
+/* ---------------------------------------------------- weight preparation --
+ * Registration-time conversion of a packed INT4 weight [n, k/2] + fp16 group
+ * scales [n, k/128] into the resident layout the GEMM streams with TMA:
+ * int8 [.., k] (16 x code, nibble-interleaved per 32 columns) at row
+ * dst(r) = (r/block_rows)*dst_block_stride + dst_offset + r%block_rows, and
+ * fp32 scales [k/128, scale_ld] at column dst(r).  Replaces the per-call
+ * weight leases of native_runtime.cpp:84-260 (weights stay resident). */
+int k2b_prepare_weight(const void* w_packed, const void* w_scale, void* w_prepared, void* scale_t, int n, int k,
+                       int block_rows, int dst_block_stride, int dst_offset, int scale_ld, void* stream);
+
+/* -------------------------------------------------------------- W4A4 GEMM --
+ * a u8 [m,k/2] + sa fp16 [m,k/128]; w/wscale prepared; n % 256 == 0. */
+/* fp32 result p (exact group accumulation; k2b's test hook for the int32
+ * accumulators). */
+int k2b_gemm_f32(const void* a, const void* sa, const void* w, const void* wscale, void* out, int m, int n, int k,
+                 void* stream);
+/* bf16(p): the plain projection of k2_gemm4 (kernels/native_dispatch.cu:26-29). */
+int k2b_gemm_bf16(const void* a, const void* sa, const void* w, const void* wscale, void* out, int m, int n, int k,
+                  void* stream);
+
+/* Fused Q/K/V(/gate) projection: replaces k2_int4_qkv
+ * (kernels/joint_projection.cu:222-231) and the split QKGemm + k2_gemm4 group
+ * (native_runtime.cpp:333-358, kernels/qk_norm_rope.cu:135).
+ * Q, K: per-head RMSNorm (nq/nk fp32 [128], eq/ek) + adjacent-pair RoPE with
+ * freqs fp32 [length,64,2,2] (token = row % length); V: bf16(p);
+ * gate (optional, wg/go non-null): bf16(sigmoid(bf16(p))).
+ * Outputs token-major bf16: qo [m,qwidth], ko/vo [m,kvwidth], go [m,qwidth].
+ * qwidth, kvwidth multiples of 256. */
+int k2b_qkv(const void* a, const void* sa, const void* wq, const void* swq, const void* wk, const void* swk,
+            const void* wv, const void* swv, const void* wg, const void* swg, const void* nq, const void* nk,
+            const void* freqs, void* qo, void* ko, void* vo, void* go, int m, int length, int qwidth, int kvwidth,
+            int k, float eq, float ek, void* stream);
+
+/* Projection with gated residual: out = bf16(resid + bf16(bf16(p)*gate[b,c])),
+ * b = row/length; gate bf16 [batch, n], resid/out bf16 [m, n].  Replaces
+ * k2_int4_gated_residual (kernels/int4_epilogue.cu:77-85) and the
+ * output half of k2_int4_residual_norm (kernels/joint_projection.cu:178-179). */
+int k2b_gated_residual(const void* a, const void* sa, const void* w, const void* wscale, const void* gate,
+                       const void* residual, void* out, int m, int length, int n, int k, void* stream);
+
+/* Gate/up projection + SwiGLU + INT4 requant of the down-projection input:
+ * h = bf16(bf16(silu(bf16(pg)))*bf16(pu)), then H128 rotation + group-128
+ * INT4 -> hq u8 [m, width/2], hs fp16 [m, width/128].  Replaces
+ * k2_int4_swiglu (kernels/joint_projection.cu:204-211) plus the separate
+ * quantize() before the down projection (native_runtime.cpp:327).
+ * width % 128 == 0. */
+int k2b_swiglu_quant(const void* a, const void* sa, const void* wg, const void* sg, const void* wu, const void* su,
+                     void* hq, void* hs, int m, int width, int k, void* stream);
+/* As above with bf16 h [m, width] out (k2_int4_swiglu's output). */
+int k2b_swiglu_bf16(const void* a, const void* sa, const void* wg, const void* sg, const void* wu, const void* su,
+                    void* h, int m, int width, int k, void* stream);
+
+/* ------------------------------------------------------------- attention --
+ * GQA flash attention, non-causal, head_dim 128, (heads/kvheads) even.
+ * Replaces k2_fullgraph::kohaku_fa (KohakuKernelRouter/attention.py:189-193,
+ * fwd_kernel :63-110).  q [B,heads,lq,128], k/v [B,kvheads,lk,128] given by
+ * element strides (batch, head, token; last dim contiguous; all multiples of
+ * 8); out bf16 [B, lq, heads*128]; gate (optional) bf16 with out's layout,
+ * gate_kind 1 = sigmoid applied here, 2 = already sigmoided. */
+int k2b_attention(const void* q, const void* k, const void* v, const void* gate, void* out, int batch, int heads,
+                  int kvheads, int lq, int lk, int dim, long long q_sb, long long q_sh, long long q_st,
+                  long long k_sb, long long k_sh, long long k_st, long long v_sb, long long v_sh, long long v_st,
+                  int gate_kind, void* stream);
+/* Attention with the out-projection's input quantisation fused into the
+ * store: oq u8 [B*lq, heads*64], os fp16 [B*lq, heads] (one group per head). */
+int k2b_attention_quant(const void* q, const void* k, const void* v, void* oq, void* os, int batch, int heads,
+                        int kvheads, int lq, int lk, int dim, long long q_sb, long long q_sh, long long q_st,
+                        long long k_sb, long long k_sh, long long k_st, long long v_sb, long long v_sh,
+                        long long v_st, void* stream);
+
+/* ------------------------------------------------------------ block loop --
+ * Native loop over transformer blocks (replaces the compiled entry that
+ * NativeGraph::run drives, native_runtime.cpp:543-571, over graph_model.py's
+ * quant chain :108-114, :266-295).  block_ptrs holds k2b_block_slots()
+ * pointers per block in this order:
+ *   0 prenorm w (fp32 [hidden])   1 postnorm w   2 q-norm w (fp32 [128])
+ *   3 k-norm w   4/5 Wq, Sq   6/7 Wk, Sk   8/9 Wv, Sv   10/11 Wo, So
+ *   12/13 Wgate, Sgate   14/15 Wup, Sup   16/17 Wdown, Sdown
+ *   18 modulation bf16 [6, batch, hidden] = (ps, ph, pg, ss, sh, sg)
+ * (W = prepared int8, S = prepared fp32 scales).  x bf16 [batch*length,
+ * hidden] is updated in place; freqs fp32 [length,64,2,2];
+ * workspace >= k2b_block_workspace_bytes(). hidden == heads*128. */
+int k2b_block_slots(void);
+long long k2b_block_workspace_bytes(int rows, int hidden, int heads, int kvheads, int mlp);
+int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, const void* freqs, void* workspace,
+                       long long workspace_bytes, int batch, int length, int hidden, int heads, int kvheads, int mlp,
+                       float eps, float qk_eps, void* stream);
+
+/* -------------------------------------- reference-named exports (shims) --
+ * Same names and argument order as the reference's kernel libraries so that
+ * native_runtime.cpp's configure()/configure_joint()/configure_norm_quant()
+ * dlsym calls resolve unchanged; data follows the contract above.
+ * group must be 128 and dtype 2 (bf16) for k2_norm_mod_quant4; dtype 0
+ * (bf16) for the k2_int4_* family; batch 1 (length = m). */
+int k2_norm_mod_quant4(const void* x, const void* norm, const void* scale, const void* shift, void* q, void* scales,
+                       int rows, int K, int length, int cut, int batch, float eps, int group, int dtype,
+                       void* stream); /* kernels/norm_quant.cu:89-91 */
+int k2_int4_qkv(const void* a, const void* wq, const void* wk, const void* wv, const void* wg, const void* xs,
+                const void* sq, const void* sk, const void* sv, const void* sg, const void* nq, const void* nk,
+                const void* freq, void* qo, void* ko, void* vo, void* go, int m, int qwidth, int kvwidth, int k,
+                int dtype, float eq, float ek, void* stream); /* kernels/joint_projection.cu:222-225 */
+int k2_int4_swiglu(const void* a, const void* wg, const void* wu, const void* xs, const void* sg, const void* su,
+                   void* out, int m, int n, int k, int dtype, void* stream); /* kernels/joint_projection.cu:204-205 */
+int k2_int4_gated_residual(void* a, void* w, void* xs, void* ws, void* gate, void* residual, void* output, int m,
+                           int n, int k, int dtype, int config, void* stream); /* kernels/int4_epilogue.cu:77-78 */
+int k2_int4_qk_norm_rope(void* a, void* w, void* xs, void* ws, void* norm, void* freqs, void* output, int m, int n,
+                         int k, int dtype, float eps, void* stream); /* kernels/qk_norm_rope.cu:135 */
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* K2B_H */

@@ -1,0 +1,403 @@
+/*
+ * k2_oracle.c -- CPU restatement of the Krea2 W4A4 DiT block hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product links or calls this file;
+ * only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg load it,
+ * and only as the checker.
+ *
+ * Every function states the reference code it restates (paths are relative to
+ * the ComfyUI-K2-Precompile project).  Where BASELINE's contract differs from
+ * the reference (group-128 fp16 scales, normalised H128 rotation, RNE quant),
+ * the contract is the one both this file and the CUDA kernels follow; the
+ * reference's rounding points (bf16 after every modulation step, fp32 fmaf
+ * chains) are kept.
+ *
+ * Parity status: the rotation/quantisation helpers of the reference live in the
+ * un-vendored comfy-kitchen sources, so the INT4 contract here is pinned by this
+ * restatement and by golden fixtures of the reference's own Triton kernels
+ * (norm/modulation, QK-norm+RoPE, SiLU product, attention) run under the Triton
+ * interpreter; see tests/golden/make_golden.py.
+ *
+ * Build: gcc -O3 -ffp-contract=off -fno-fast-math -shared -fPIC
+ * (oracle/Makefile).  fp contraction must stay off: every fused multiply-add
+ * below is an explicit fmaf(), every other operation rounds to fp32.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---------------------------------------------------------------- numerics */
+
+static inline float bits_f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+float k2o_bf16_to_f32(uint16_t h) { return bits_f((uint32_t)h << 16); }
+
+/* round-to-nearest-even fp32 -> bf16 (NaN kept quiet), like __float2bfloat16_rn */
+uint16_t k2o_f32_to_bf16(float f) {
+    uint32_t u = f_bits(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static inline float bf(uint16_t h) { return k2o_bf16_to_f32(h); }
+static inline float bfr(float f) { return k2o_bf16_to_f32(k2o_f32_to_bf16(f)); }
+
+/* IEEE binary16 conversions (round-to-nearest-even), like __float2half_rn */
+uint16_t k2o_f32_to_f16(float f) {
+    _Float16 h = (_Float16)f;
+    uint16_t u; memcpy(&u, &h, 2); return u;
+}
+float k2o_f16_to_f32(uint16_t u) {
+    _Float16 h; memcpy(&h, &u, 2); return (float)h;
+}
+
+/* correctly rounded 1/sqrt(x) (the CUDA side calls __frsqrt_rn) */
+float k2o_rsqrt_rn(float x) { return (float)(1.0L / sqrtl((long double)x)); }
+
+/*
+ * exp(x) in fp32 from basic correctly-rounded operations only, so that the CUDA
+ * kernels (same sequence, __fmaf_rn/__fmul_rn) produce identical bits.
+ * Method: Cody-Waite range reduction x = n*ln2 + r with a two-part ln2 (the
+ * split used by fdlibm's e_expf.c), Taylor polynomial of degree 7 in Horner
+ * form (|r| <= ln2/2 -> truncation error < 0.2 ulp), scaling by 2^n through
+ * the exponent field.  Max error vs a correctly rounded exp: ~2 ulp.
+ */
+float k2o_exp(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.972084045410156f) return 0.0f;
+    float n = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(n, -0.693145751953125f, x);
+    r = fmaf(n, -1.428606765330187045037746429443359375e-06f, r);
+    float p = 1.98412698412698412526e-4f;
+    p = fmaf(p, r, 1.38888888888888894189e-3f);
+    p = fmaf(p, r, 8.33333333333333321769e-3f);
+    p = fmaf(p, r, 4.16666666666666643537e-2f);
+    p = fmaf(p, r, 1.66666666666666657415e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int e = (int)n;
+    if (e > 127) { p = p * 1.7014118346046923e38f; e -= 127; }      /* 2^127 */
+    if (e < -126) { p = p * 1.1754943508222875e-38f; e += 126; }    /* 2^-126 */
+    return p * bits_f((uint32_t)(e + 127) << 23);
+}
+
+/* SiLU and sigmoid as kernels/joint_projection.cu:95 and :136 write them
+ * (x / (1 + exp(-x)), 1 / (1 + exp(-x))), with k2o_exp for exp. */
+float k2o_silu(float x) { return x / (1.0f + k2o_exp(-x)); }
+float k2o_sigmoid(float x) { return 1.0f / (1.0f + k2o_exp(-x)); }
+
+/* ------------------------------------------------ rotation + INT4 packing */
+
+/* fp32(1/sqrt(128)): the normalisation of the Sylvester H128 block. */
+#define K2_HSCALE 0.0883883461356163024902343750f
+
+/* In-place Sylvester Walsh-Hadamard transform of 128 fp32 values, stages
+ * h = 1, 2, 4, ..., 64; (a, b) -> (a + b, a - b).  Then scaled by K2_HSCALE.
+ * This is the contract's "normalised 128x128 block-Hadamard".
+ * The reference rotates with comfy-kitchen's ConvRot stages
+ * (kernels/norm_quant.cu:40-60); those helpers are not vendored. */
+void k2o_hadamard128(float* v) {
+    for (int h = 1; h < 128; h <<= 1)
+        for (int i = 0; i < 128; i += 2 * h)
+            for (int j = i; j < i + h; ++j) {
+                float a = v[j], b = v[j + h];
+                v[j] = a + b;
+                v[j + h] = a - b;
+            }
+    for (int j = 0; j < 128; ++j) v[j] = v[j] * K2_HSCALE;
+}
+
+/* Quantise one rotated group of 128: scale = fp16(absmax / 7), codes =
+ * clamp(rne(v / scale), -8, 7) (correctly rounded division), two codes per
+ * byte, low nibble = even column.  Follows the role of kitchen's
+ * finite_absmax_for_int4_scale / quantize_int4_pack4_word
+ * (kernels/norm_quant.cu:61-66) with BASELINE's group-128 fp16 scale. */
+void k2o_quant_group128(const float* v, uint8_t* q, uint16_t* s) {
+    float amax = 0.0f;
+    for (int j = 0; j < 128; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    float sf = amax / 7.0f;
+    if (sf > 65504.0f) sf = 65504.0f;
+    uint16_t sh = k2o_f32_to_f16(sf);
+    float sd = k2o_f16_to_f32(sh);
+    *s = sh;
+    for (int j = 0; j < 128; j += 2) {
+        int c[2];
+        for (int t = 0; t < 2; ++t) {
+            float r = sd > 0.0f ? rintf(v[j + t] / sd) : 0.0f;
+            if (r > 7.0f) r = 7.0f;
+            if (r < -8.0f) r = -8.0f;
+            c[t] = (int)r;
+        }
+        q[j / 2] = (uint8_t)((c[0] & 0xf) | ((c[1] & 0xf) << 4));
+    }
+}
+
+/* ------------------------------------------------------------- norm_quant */
+
+/* Reduction order of kernels/norm_quant.cu:20-31 (ATen's vectorised RMSNorm):
+ * 128 lanes, lane t accumulates fmaf(v, v, sum) over columns t*4 + j + 512*i
+ * (j inner), a shfl_down tree (16, 8, 4, 2, 1) inside each warp of 32 lanes,
+ * then (w2 + w0) + (w3 + w1). */
+static float row_sumsq(const uint16_t* x, int K) {
+    float warp[4];
+    for (int w = 0; w < 4; ++w) {
+        float lane[32];
+        for (int l = 0; l < 32; ++l) {
+            int t = 32 * w + l;
+            float sum = 0.0f;
+            for (int col = t * 4; col < K; col += 512)
+                for (int j = 0; j < 4; ++j) {
+                    float v = col + j < K ? bf(x[col + j]) : 0.0f;
+                    sum = fmaf(v, v, sum);
+                }
+            lane[l] = sum;
+        }
+        for (int off = 16; off; off >>= 1)
+            for (int l = 0; l < off; ++l) lane[l] = lane[l] + lane[l + off];
+        warp[w] = lane[0];
+    }
+    return (warp[2] + warp[0]) + (warp[3] + warp[1]);
+}
+
+/* Batch row of the modulation vectors, kernels/norm_quant.cu:32. */
+static int mod_row(int row, int length, int cut, int batch) {
+    int b = row / length;
+    if (cut >= 0 && row % length >= cut) b += batch;
+    return b;
+}
+
+/*
+ * Fused RMSNorm -> adaLN modulation -> H128 rotation -> group-128 INT4 pack.
+ * Restates kernels/norm_quant.cu:11-67 (norm_mod_quant) with BASELINE's
+ * rotation and scale layout:
+ *   inv = rsqrt_rn(sum/K + eps)                          (:30-31)
+ *   y   = bf16((x*inv)*(w+1))                            (:34)
+ *   f   = bf16(scale+1); y = bf16(y*f); v = bf16(y+shift) (:35-37)
+ * x bf16 [rows,K]; w fp32 [K] (the "w+1" form, native_schedule.py:252-253);
+ * scale/shift bf16 [nbatch,K]; q u8 [rows,K/2]; s fp16 [rows,K/128].
+ */
+int k2o_norm_quant(const uint16_t* x, const float* w, const uint16_t* scale,
+                   const uint16_t* shift, uint8_t* q, uint16_t* s, int rows, int K,
+                   int length, int cut, int batch, float eps) {
+    if (rows <= 0 || K <= 0 || K % 128 || length <= 0) return 1;
+    for (int row = 0; row < rows; ++row) {
+        const uint16_t* xr = x + (int64_t)row * K;
+        float* v = (float*)malloc(sizeof(float) * (size_t)K);
+        float sum = row_sumsq(xr, K);
+        float inv = k2o_rsqrt_rn(sum / (float)K + eps);
+        int b = mod_row(row, length, cut, batch);
+        for (int col = 0; col < K; ++col) {
+            float t = bf(xr[col]) * inv;
+            float w1 = w[col] + 1.0f;
+            float y = bfr(t * w1);
+            float f = bfr(bf(scale[(int64_t)b * K + col]) + 1.0f);
+            y = bfr(y * f);
+            v[col] = bfr(y + bf(shift[(int64_t)b * K + col]));
+        }
+        for (int g = 0; g < K / 128; ++g) {
+            k2o_hadamard128(v + g * 128);
+            k2o_quant_group128(v + g * 128, q + (int64_t)row * (K / 2) + g * 64,
+                               s + (int64_t)row * (K / 128) + g);
+        }
+        free(v);
+    }
+    return 0;
+}
+
+/* The RMSNorm + modulation half of k2o_norm_quant alone (bf16 out): the
+ * semantics of kernels/native_dispatch.cu:44-62 (norm_mod) and the Triton
+ * twin forward_kernels.py:13-45 (_norm_mod), with the reduction order above. */
+int k2o_norm_mod(const uint16_t* x, const float* w, const uint16_t* scale, const uint16_t* shift,
+                 uint16_t* out, int rows, int K, int length, int cut, int batch, float eps) {
+    if (rows <= 0 || K <= 0 || length <= 0) return 1;
+    for (int row = 0; row < rows; ++row) {
+        const uint16_t* xr = x + (int64_t)row * K;
+        float sum = row_sumsq(xr, K);
+        float inv = k2o_rsqrt_rn(sum / (float)K + eps);
+        int b = mod_row(row, length, cut, batch);
+        for (int col = 0; col < K; ++col) {
+            float t = bf(xr[col]) * inv;
+            float w1 = w[col] + 1.0f;
+            float y = bfr(t * w1);
+            float f = bfr(bf(scale[(int64_t)b * K + col]) + 1.0f);
+            y = bfr(y * f);
+            out[(int64_t)row * K + col] = k2o_f32_to_bf16(y + bf(shift[(int64_t)b * K + col]));
+        }
+    }
+    return 0;
+}
+
+/* Rotation + quantisation of an already-formed bf16 activation (the input
+ * quantisation that native_runtime.cpp:268-271 `quantize` performs before the
+ * out-projection), BASELINE contract. */
+int k2o_rotate_quant(const uint16_t* x, uint8_t* q, uint16_t* s, int rows, int K) {
+    if (rows <= 0 || K <= 0 || K % 128) return 1;
+    for (int row = 0; row < rows; ++row) {
+        float v[128];
+        for (int g = 0; g < K / 128; ++g) {
+            for (int j = 0; j < 128; ++j) v[j] = bf(x[(int64_t)row * K + g * 128 + j]);
+            k2o_hadamard128(v);
+            k2o_quant_group128(v, q + (int64_t)row * (K / 2) + g * 64,
+                               s + (int64_t)row * (K / 128) + g);
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------- W4A4 GEMM */
+
+static void unpack_row(const uint8_t* p, int8_t* out, int K) {
+    for (int i = 0; i < K / 2; ++i) {
+        int lo = p[i] & 0xf, hi = p[i] >> 4;
+        out[2 * i] = (int8_t)(lo >= 8 ? lo - 16 : lo);
+        out[2 * i + 1] = (int8_t)(hi >= 8 ? hi - 16 : hi);
+    }
+}
+
+/*
+ * Group-scaled W4A4 GEMM, fp32 result p[r,c] for the selected rows.
+ * Accumulation: int32 per (row, 128-wide K group) as the s4 mma of
+ * kernels/joint_projection.cu:51-56 produces; dequant of the contract
+ * (group-128 scales on both operands; the reference's per-row/per-channel
+ * version is T(float(acc)*xs*ws), kernels/joint_projection.cu:57-59):
+ *     p = 0;  for g:  u = fp32(float(acc_g) * sA[r,g]);  p = fmaf(u, sW[c,g], p)
+ * A u8 [M,K/2] + fp16 [M,K/128]; W u8 [N,K/2] + fp16 [N,K/128].
+ * rows == NULL selects rows 0..nrows-1.  out fp32 [nrows, N].
+ * acc_out (optional) receives the int32 accumulators [nrows, N, K/128].
+ */
+int k2o_gemm_w4a4(const uint8_t* A, const uint16_t* sA, const uint8_t* W, const uint16_t* sW,
+                  int M, int N, int K, const int* rows, int nrows, float* out, int32_t* acc_out) {
+    if (K % 128 || M <= 0 || N <= 0) return 1;
+    int G = K / 128;
+    int8_t* wu = (int8_t*)malloc((size_t)N * K);
+    float* swf = (float*)malloc(sizeof(float) * (size_t)N * G);
+    for (int c = 0; c < N; ++c) {
+        unpack_row(W + (int64_t)c * (K / 2), wu + (int64_t)c * K, K);
+        for (int g = 0; g < G; ++g) swf[(int64_t)c * G + g] = k2o_f16_to_f32(sW[(int64_t)c * G + g]);
+    }
+    for (int i = 0; i < nrows; ++i) {
+        int r = rows ? rows[i] : i;
+        int8_t* au = (int8_t*)malloc((size_t)K);
+        float* saf = (float*)malloc(sizeof(float) * (size_t)G);
+        unpack_row(A + (int64_t)r * (K / 2), au, K);
+        for (int g = 0; g < G; ++g) saf[g] = k2o_f16_to_f32(sA[(int64_t)r * G + g]);
+        for (int c = 0; c < N; ++c) {
+            const int8_t* wr = wu + (int64_t)c * K;
+            float p = 0.0f;
+            for (int g = 0; g < G; ++g) {
+                int32_t acc = 0;
+                for (int k = 0; k < 128; ++k) acc += (int32_t)au[g * 128 + k] * (int32_t)wr[g * 128 + k];
+                if (acc_out) acc_out[((int64_t)i * N + c) * G + g] = acc;
+                float u = (float)acc * saf[g];
+                p = fmaf(u, swf[(int64_t)c * G + g], p);
+            }
+            out[(int64_t)i * N + c] = p;
+        }
+        free(au);
+        free(saf);
+    }
+    free(wu);
+    free(swf);
+    return 0;
+}
+
+/* ------------------------------------------------------------- epilogues */
+
+/* Per-head RMSNorm over 128 channels with the reduction order of
+ * kernels/joint_projection.cu:141-146 (lane l holds channels 4l..4l+3, fmaf in
+ * j order, shfl_down tree, lane 0's total), then adjacent-pair RoPE
+ * (:147-152):  a = bf16((v*inv)*(w+1)), o0 = bf16(fmaf(f0,a,f1*b)),
+ * o1 = bf16(fmaf(f2,a,f3*b)).  v = bf16(p) is the rounded projection (:134).
+ * p fp32 [nrows, ld] (cols [0, heads*128) used); normw fp32 [128];
+ * freqs fp32 [L,64,2,2]; token = row_index % L; out bf16 [nrows, heads*128]. */
+int k2o_qk_norm_rope(const float* p, int nrows, int ld, int heads, const float* normw, float eps,
+                     const float* freqs, int L, const int* rows, uint16_t* out) {
+    for (int i = 0; i < nrows; ++i) {
+        int r = rows ? rows[i] : i;
+        int token = r % L;
+        for (int h = 0; h < heads; ++h) {
+            float v[128];
+            for (int j = 0; j < 128; ++j) v[j] = bfr(p[(int64_t)i * ld + h * 128 + j]);
+            float lane[32];
+            for (int l = 0; l < 32; ++l) {
+                float s = 0.0f;
+                for (int j = 0; j < 4; ++j) s = fmaf(v[4 * l + j], v[4 * l + j], s);
+                lane[l] = s;
+            }
+            for (int off = 16; off; off >>= 1)
+                for (int l = 0; l < off; ++l) lane[l] = lane[l] + lane[l + off];
+            float inv = k2o_rsqrt_rn(lane[0] / 128.0f + eps);
+            for (int pr = 0; pr < 64; ++pr) {
+                int c = 2 * pr;
+                float a = bfr((v[c] * inv) * (normw[c] + 1.0f));
+                float b = bfr((v[c + 1] * inv) * (normw[c + 1] + 1.0f));
+                const float* f = freqs + ((int64_t)token * 64 + pr) * 4;
+                uint16_t* o = out + (int64_t)i * heads * 128 + h * 128 + c;
+                o[0] = k2o_f32_to_bf16(fmaf(f[0], a, f[1] * b));
+                o[1] = k2o_f32_to_bf16(fmaf(f[2], a, f[3] * b));
+            }
+        }
+    }
+    return 0;
+}
+
+/* Gated residual of kernels/int4_epilogue.cu:24-37 / joint_projection.cu:178-179:
+ * out = bf16(resid + bf16(bf16(p) * gate[b,c])), b = row / length.
+ * p fp32 [nrows,N]; gate bf16 [nbatch,N]; resid/out bf16 [nrows,N]. */
+int k2o_gated_residual(const float* p, int nrows, int N, const uint16_t* gate,
+                       const uint16_t* resid, int length, const int* rows, uint16_t* out) {
+    for (int i = 0; i < nrows; ++i) {
+        int r = rows ? rows[i] : i;
+        int b = r / length;
+        for (int c = 0; c < N; ++c) {
+            float pv = bfr(p[(int64_t)i * N + c]);
+            float g = bfr(pv * bf(gate[(int64_t)b * N + c]));
+            out[(int64_t)i * N + c] = k2o_f32_to_bf16(bf(resid[(int64_t)i * N + c]) + g);
+        }
+    }
+    return 0;
+}
+
+/* SwiGLU of kernels/joint_projection.cu:94-96 (g = bf16(pg), u = bf16(pu),
+ * a = bf16(silu(g)), h = bf16(a*u)) followed by the contract's fused input
+ * quantisation of the down projection (H128 rotation + group-128 INT4).
+ * pg/pu fp32 [nrows,F]; hq u8 [nrows,F/2]; hs fp16 [nrows,F/128];
+ * h (optional) bf16 [nrows,F]. */
+int k2o_swiglu_quant(const float* pg, const float* pu, int nrows, int F, uint8_t* hq,
+                     uint16_t* hs, uint16_t* h) {
+    if (F % 128) return 1;
+    for (int i = 0; i < nrows; ++i) {
+        float v[128];
+        for (int g = 0; g < F / 128; ++g) {
+            for (int j = 0; j < 128; ++j) {
+                int64_t idx = (int64_t)i * F + g * 128 + j;
+                float gv = bfr(pg[idx]);
+                float uv = bfr(pu[idx]);
+                float a = bfr(k2o_silu(gv));
+                v[j] = bfr(a * uv);
+                if (h) h[idx] = k2o_f32_to_bf16(v[j]);
+            }
+            k2o_hadamard128(v);
+            k2o_quant_group128(v, hq + (int64_t)i * (F / 2) + g * 64, hs + (int64_t)i * (F / 128) + g);
+        }
+    }
+    return 0;
+}
+
+/* Attention gate of kernels/joint_projection.cu:136: bf16(sigmoid(bf16(p))). */
+int k2o_sigmoid_gate(const float* p, int64_t n, uint16_t* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = k2o_f32_to_bf16(k2o_sigmoid(bfr(p[i])));
+    return 0;
+}
+
+/* Vectorised helpers for the Python side. */
+void k2o_exp_vec(const float* x, float* y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = k2o_exp(x[i]);
+}
+void k2o_bf16_round_vec(const float* x, uint16_t* y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = k2o_f32_to_bf16(x[i]);
+}
