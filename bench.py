@@ -1,0 +1,519 @@
+#!/usr/bin/env python
+"""Benchmark of the Krea2 W4A4 DiT block hot path on B200 (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: 8 independent latents x 4224 tokens
+(128 text + 64x64 image), 28 Krea2-shaped W4A4 blocks (hidden 6144, 48/12
+heads, MLP 16384), random-init weights (N(0,0.02), H128-rotated, INT4),
+synthetic N(0,1) hidden states.  One step = the 28-block forward of all 8
+latents; with N ranks each rank runs 8/N latents (batch sharding, no
+collective: "scaling": "strong" over the fixed 8-latent job).  The metric's
+other half, the 28-block forward at 4050 tokens batch 1 (config 3), is
+measured on rank 0 at N=1 and reported as "forward_ms_4050".
+
+value: latents/s with inputs resident in HBM.  e2e: the same through the
+public forward with the step's hidden states copied host->device from pinned
+memory and the result copied back inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "comfyui-k2-precompile_b200"))
+
+METRIC = "W4A4 DiT forward ms @4050 tok x28 blocks; latents/s at 1/2/4/8 B200"
+LATENTS = 8
+TEXT, GRID = 128, 64
+LENGTH = TEXT + GRID * GRID  # 4224
+OP_NAMES = ["norm_quant_pre", "qkv_qknorm_rope", "attention_quant", "out_proj_residual", "norm_quant_post",
+            "gate_up_swiglu_quant", "down_proj_residual"]
+
+
+def _env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+# ------------------------------------------------------------ CPU baseline
+
+def cpu_sample_latent_seconds(rows_sample: int = 8, seed: int = 0):
+    """Times the CPU oracle (oracle/, a C + numpy restatement of the reference
+    path) on `rows_sample` token rows of one config-4 latent through every
+    stage of one block, and extrapolates to seconds per latent forward
+    (x 4224/rows_sample rows x 28 blocks).  Returns (seconds, threads, note)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    rng = np.random.default_rng(seed)
+    H, F, heads, kvh = 6144, 16384, 48, 12
+
+    def pw(n, k):  # packed weight + fp16 scales (values irrelevant to timing)
+        return (rng.integers(0, 256, (n, k // 2), dtype=np.uint8),
+                (rng.uniform(0.001, 0.01, (n, k // 128)).astype(np.float16)).view(np.uint16))
+
+    W = {"q": pw(heads * 128, H), "k": pw(kvh * 128, H), "v": pw(kvh * 128, H), "o": pw(H, H),
+         "g": pw(F, H), "u": pw(F, H), "d": pw(H, F)}
+    x = O.bf16_bits(rng.standard_normal((rows_sample, H)).astype(np.float32))
+    w = np.zeros(H, np.float32)
+    mod = O.bf16_bits(rng.normal(0, 0.1, (6, 1, H)).astype(np.float32))
+    normw = np.zeros(128, np.float32)
+    pos = np.stack([np.arange(LENGTH), np.arange(LENGTH)], 1).astype(np.float32)
+    freqs = O.rope_table(pos, (64, 64), 10000.0)
+    kv = O.bf16_bits(rng.standard_normal((1, kvh, LENGTH, 128)).astype(np.float32))
+    O.lib()
+    t0 = time.perf_counter()
+    xq, xs = O.norm_quant(x, w, mod[0], mod[1])
+    pq = O.gemm_w4a4(xq, xs, *W["q"])
+    pk = O.gemm_w4a4(xq, xs, *W["k"])
+    pv = O.gemm_w4a4(xq, xs, *W["v"])
+    q = O.qk_norm_rope(pq, heads, normw, 1e-6, freqs, LENGTH)
+    O.qk_norm_rope(pk, kvh, normw, 1e-6, freqs, LENGTH)
+    O.bf16_bits(pv)
+    q4 = q.reshape(1, rows_sample, heads, 128).transpose(0, 2, 1, 3)
+    o = O.attention(q4, kv, kv).reshape(rows_sample, H)
+    oq, os_ = O.rotate_quant(o)
+    x1 = O.gated_residual(O.gemm_w4a4(oq, os_, *W["o"]), mod[2], x, rows_sample)
+    hq_in, hs_in = O.norm_quant(x1, w, mod[3], mod[4])
+    hq, hs = O.swiglu_quant(O.gemm_w4a4(hq_in, hs_in, *W["g"]), O.gemm_w4a4(hq_in, hs_in, *W["u"]))
+    O.gated_residual(O.gemm_w4a4(hq, hs, *W["d"]), mod[5], x1, rows_sample)
+    dt = time.perf_counter() - t0
+    per_latent = dt * (LENGTH / rows_sample) * 28
+    note = (f"oracle/ C+numpy port, one block on {rows_sample} of {LENGTH} token rows of one latent "
+            f"(all 7 stages, attention over all {LENGTH} keys), {dt:.2f} s, scaled x{LENGTH // rows_sample} rows x28 blocks")
+    return per_latent, O._workers(), note
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference path's CPU restatement (the reference's
+    own kernels are SM89 CUDA + un-vendored comfy-kitchen and cannot build
+    here), timed on the host cores.  Each step is one bounded sample."""
+    if rank != 0:
+        return
+    samples = []
+    threads, note = 1, ""
+    for i in range(args.warmup + args.steps):
+        sec, threads, note = cpu_sample_latent_seconds(rows_sample=48, seed=i)
+        if i >= args.warmup:
+            samples.append(sec)
+    per_latent = statistics.median(samples)
+    value = 1.0 / per_latent
+    line = {
+        "metric": METRIC, "value": value, "unit": "latents/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_latent * LATENTS * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "w4a4-int/bf16",
+        "data": "synthetic",
+        "config": {"workload": "config 4: 8 latents x 4224 tokens, 28 blocks (CPU: sampled rows, extrapolated)",
+                   "latents": LATENTS, "tokens": LENGTH, "blocks": 28, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "latents/s", "cores": threads, "kind": "port", "sample": note},
+        "e2e": {"value": value, "unit": "latents/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- GPU helpers
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = set(indices)
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if self.indices and idx not in self.indices:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                mx = float(parts[2].split()[0])
+                power.append(float(parts[3].split()[0]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def int8_peak_tops(torch):
+    """Dense int8 tensor throughput measured here: torch._int_mm (cuBLASLt)
+    8192^3, best of 10 with CUDA events."""
+    n = 8192
+    a = torch.randint(-8, 8, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-8, 8, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def load_traffic():
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# ------------------------------------------------- single-kernel profiling
+
+def run_kernel_case(args):
+    """--kernel NAME: launches one kernel of the block on a small synthetic
+    case (one latent by default) `--reps` times; used for ncu captures."""
+    import torch
+
+    from k2b import ops
+    from k2b.model import ModelConfig, quantize_weight, rope_positions, rope_table
+
+    cfg = ModelConfig()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rows = args.rows
+    g = torch.Generator(device=dev).manual_seed(5)
+    H, F = cfg.hidden, cfg.mlp
+
+    def weight(n, k):
+        q, s = quantize_weight((torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        return ops.prepare_weight(q, s)
+
+    x = torch.randn((rows, H), generator=g, device=dev).to(torch.bfloat16)
+    w = torch.zeros(H, device=dev)
+    mod = (torch.randn((6, 1, H), generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    xq, xs = ops.norm_quant(x, w, mod[0], mod[1])
+    name = args.kernel
+    if name == "norm_quant":
+        fn = lambda: ops.norm_quant(x, w, mod[0], mod[1])
+    elif name == "qkv":
+        wq, wk, wv = weight(cfg.heads * 128, H), weight(cfg.kvheads * 128, H), weight(cfg.kvheads * 128, H)
+        L = rows
+        freqs = rope_table(rope_positions(L % 64, L // 64, 64), (64, 64)).to(dev)
+        nw = torch.zeros(128, device=dev)
+        fn = lambda: ops.qkv(xq, xs, wq, wk, wv, nw, nw, freqs, length=L)
+    elif name == "out_proj":
+        wo = weight(H, H)
+        fn = lambda: ops.gated_residual(xq, xs, wo, mod[2], x, length=rows)
+    elif name == "gate_up":
+        wg, wu = weight(F, H), weight(F, H)
+        fn = lambda: ops.swiglu_quant(xq, xs, wg, wu)
+    elif name == "down":
+        wd = weight(H, F)
+        hq = torch.randint(0, 256, (rows, F // 2), dtype=torch.uint8, device=dev)
+        hs = torch.full((rows, F // 128), 0.01, dtype=torch.float16, device=dev)
+        fn = lambda: ops.gated_residual(hq, hs, wd, mod[5], x, length=rows)
+    elif name == "attention":
+        q = torch.randn((1, cfg.heads, rows, 128), device=dev).to(torch.bfloat16)
+        k = torch.randn((1, cfg.kvheads, rows, 128), device=dev).to(torch.bfloat16)
+        fn = lambda: ops.attention_quant(q, k, k)
+    else:
+        raise SystemExit(f"unknown kernel {name}")
+    fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel": name, "rows": rows, "reps": args.reps,
+                      "avg_us": s.elapsed_time(e) * 1e3 / args.reps}), flush=True)
+
+
+# --------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", default=None,
+                    help="profile mode: norm_quant|qkv|out_proj|gate_up|down|attention on one small case")
+    ap.add_argument("--rows", type=int, default=LENGTH)
+    ap.add_argument("--reps", type=int, default=3)
+    args = ap.parse_args()
+    if args.kernel:
+        run_kernel_case(args)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local_rank = _env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from k2b import ops
+    from k2b.model import Krea2Blocks, ModelConfig, block_flops, rope_positions, rope_table, synthetic_blocks
+
+    if LATENTS % world:
+        raise SystemExit("the 8-latent job splits across 1, 2, 4 or 8 ranks")
+    local = LATENTS // world
+    cfg = ModelConfig()
+    peaks, peak_kind = measured_peaks()
+    int8_tops = int8_peak_tops(torch) if rank == 0 else None
+
+    blocks = synthetic_blocks(cfg, local, seed=1234, device=dev)
+    freqs = rope_table(rope_positions(TEXT, GRID, GRID), (64, 64), cfg.theta).to(dev)
+    model = Krea2Blocks(cfg, blocks, local, LENGTH, device=dev)
+    rows = local * LENGTH
+    gen = torch.Generator(device="cpu").manual_seed(77 + rank)
+    x_host = torch.randn((rows, cfg.hidden), generator=gen).to(torch.bfloat16).pin_memory()
+    x0 = x_host.to(dev)
+    x = torch.empty_like(x0)
+    out_host = torch.empty_like(x_host).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------------------------------------------- device-resident timing
+    nb = cfg.blocks
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(8 * nb)] for _ in range(args.steps)]
+    for ev in events:  # create the CUDA events before their handles are passed down
+        for e in ev:
+            e.record()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        x.copy_(x0)
+        model.forward_(x, freqs)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler([local_rank] if world == 1 else range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        x.copy_(x0)
+        model.forward_(x, freqs, events=events[i])
+    end.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+    err = ops.device_error(reset=True)
+    if err:
+        raise SystemExit(f"device-side wait gave up (error word {err})")
+    ms_per_step = elapsed_ms / args.steps
+    value = LATENTS / (ms_per_step / 1e3)
+
+    # per-kernel durations inside the timed region
+    per_op = {n: [] for n in OP_NAMES}
+    for ev in events:
+        for b in range(nb):
+            for i, n in enumerate(OP_NAMES):
+                per_op[n].append(ev[8 * b + i].elapsed_time(ev[8 * b + i + 1]))
+    total_ms = sum(sum(v) for v in per_op.values())
+    fl = block_flops(cfg, rows, LENGTH, local)
+    work = {"norm_quant_pre": None, "qkv_qknorm_rope": fl["qkv"], "attention_quant": fl["attn"],
+            "out_proj_residual": fl["out"], "norm_quant_post": None, "gate_up_swiglu_quant": fl["gate_up"],
+            "down_proj_residual": fl["down"]}
+    nq_bytes = rows * cfg.hidden * 2 + cfg.hidden * 4 + 2 * local * cfg.hidden * 2 + rows * cfg.hidden // 2 + \
+        rows * (cfg.hidden // 128) * 2
+    kernels = {}
+    for n, ts in per_op.items():
+        avg = statistics.mean(ts)
+        d = {"launches": len(ts), "avg_us": avg * 1e3, "share": sum(ts) / total_ms}
+        if n.startswith("norm_quant"):
+            d["achieved"] = nq_bytes / (avg * 1e-3) / 1e9
+            d["unit"] = "GB/s"
+            d["frac"] = d["achieved"] / peaks["hbm_gbs"]
+        elif n == "attention_quant":
+            d["achieved"] = work[n] / (avg * 1e-3) / 1e12
+            d["unit"] = "TFLOP/s"
+            d["frac"] = d["achieved"] / peaks["bf16_tflops_sustained"]
+        else:
+            d["achieved"] = work[n] / (avg * 1e-3) / 1e12
+            d["unit"] = "TOP/s int"
+            if int8_tops:
+                d["frac_of_int8_measured"] = d["achieved"] / int8_tops
+            d["frac_of_int8_datasheet"] = d["achieved"] / 4500.0
+        kernels[n] = d
+    dom = max(kernels, key=lambda k: kernels[k]["share"])
+    traffic = load_traffic().get(dom)
+
+    # ------------------------------------------------------------ end to end
+    for _ in range(args.warmup):
+        x.copy_(x_host, non_blocking=True)
+        model.forward_(x, freqs)
+        out_host.copy_(x, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        x.copy_(x_host, non_blocking=True)
+        model.forward_(x, freqs)
+        out_host.copy_(x, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2)) / args.steps
+    e2e_value = LATENTS / (e2e_ms / 1e3)
+    finite = bool(torch.isfinite(out_host.float()).all())
+
+    # ------------------------------------------- config 3 (4050 tok, batch 1)
+    fwd4050 = None
+    if world == 1:
+        L3 = 4050
+        import copy
+
+        b3 = []
+        for b in blocks:
+            c = copy.copy(b)
+            c.mod = b.mod[:, :1].contiguous()
+            b3.append(c)
+        m3 = Krea2Blocks(cfg, b3, 1, L3, device=dev)
+        f3 = rope_table(rope_positions(98, 76, 52), (64, 64), cfg.theta).to(dev)
+        x3 = x0[:L3].clone()
+        x3w = torch.empty_like(x3)
+        for _ in range(args.warmup):
+            x3w.copy_(x3)
+            m3.forward_(x3w, f3)
+        torch.cuda.synchronize()
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for _ in range(args.steps):
+            x3w.copy_(x3)
+            m3.forward_(x3w, f3)
+        e3.record()
+        torch.cuda.synchronize()
+        fwd4050 = s3.elapsed_time(e3) / args.steps
+        del m3, x3, x3w
+
+    # ------------------------------------------------------------ CPU baseline
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, threads, note = cpu_sample_latent_seconds(rows_sample=128)
+        cpu = {"value": 1.0 / sec, "unit": "latents/s", "cores": threads, "kind": "port", "sample": note}
+
+    if rank == 0:
+        kd = kernels[dom]
+        roof = {"kernel": dom, "bound": "tensor", "achieved": kd["achieved"],
+                "peak": int8_tops, "unit": "TOP/s int8",
+                "peak_source": "measured here: torch._int_mm (cuBLASLt) int8 8192^3 best of 10",
+                "frac": kd.get("frac_of_int8_measured"),
+                "frac_of_datasheet_4500": kd.get("frac_of_int8_datasheet"),
+                "traffic": traffic,
+                "work_per_launch": work[dom], "avg_launch_us": kd["avg_us"]}
+        line = {
+            "metric": METRIC, "value": value, "unit": "latents/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "w4a4-s8xs8->s32 / bf16 attention", "data": "synthetic",
+            "config": {"workload": "config 4: 8 latents x 4224 tokens (128 text + 64x64 image), 28 Krea2 blocks",
+                       "latents": LATENTS, "tokens_per_latent": LENGTH, "blocks": cfg.blocks,
+                       "hidden": cfg.hidden, "heads": cfg.heads, "kvheads": cfg.kvheads, "mlp": cfg.mlp,
+                       "parallelism": f"batch-shard x{world}", "latents_per_gpu": local,
+                       "l2": "inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"},
+            "forward_ms_4050": fwd4050,
+            "e2e": {"value": e2e_value, "unit": "latents/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": x_host.numel() * 2 * world,
+                    "d2h_bytes_per_step": out_host.numel() * 2 * world},
+            "roofline": roof,
+            "kernels": kernels,
+            "peaks": {"hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops": peaks.get("bf16_tflops"),
+                      "bf16_tflops_sustained": peaks.get("bf16_tflops_sustained"), "source": peak_kind,
+                      "int8_tops": int8_tops},
+            "gpu_launches": 7 * cfg.blocks * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "output_finite": finite,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

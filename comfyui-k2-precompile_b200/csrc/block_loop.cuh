@@ -18,6 +18,21 @@
 namespace k2b {
 static inline size_t ws_align(size_t v) { return (v + 255) & ~size_t(255); }
 
+// Events handed in by the caller may belong to another CUDA runtime instance
+// (e.g. torch's); recording them through the driver API works for any.
+typedef CUresult (*EventRecordFn)(CUevent, CUstream);
+static EventRecordFn event_record_fn() {
+  static EventRecordFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuEventRecord", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EventRecordFn>(p);
+  }
+  return fn;
+}
+
 struct BlockWorkspace {
   uint8_t* xq; __half* xs;
   __nv_bfloat16 *q, *k, *v;
@@ -76,7 +91,8 @@ K2B_EXPORT int k2b_block_slots(void) { return K2B_BLOCK_SLOTS; }
 
 K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, const void* freqs,
                                   void* workspace, long long workspace_bytes, int batch, int length, int hidden,
-                                  int heads, int kvheads, int mlp, float eps, float qk_eps, void* stream) {
+                                  int heads, int kvheads, int mlp, float eps, float qk_eps, void* const* events,
+                                  void* stream) {
   using namespace k2b;
   if (!block_ptrs || nblocks <= 0 || !x || !freqs || !workspace || batch <= 0 || length <= 0 ||
       hidden != heads * 128 || kvheads <= 0 || mlp <= 0)
@@ -93,26 +109,43 @@ K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, vo
     const size_t bh = (size_t)batch * hidden;
     const __nv_bfloat16 *ps = mod, *ph = mod + bh, *pg = mod + 2 * bh, *ss = mod + 3 * bh, *sh = mod + 4 * bh,
                         *sg = mod + 5 * bh;
-    int rc = k2b_norm_quant(x, P[K2B_SLOT_PRENORM], ps, ph, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+    // optional per-launch timing: events[blk*8 + i] is recorded before launch i
+    // (i = 0..6) and events[blk*8 + 7] after the block's last launch
+    void* const* ev = events ? events + (size_t)blk * 8 : nullptr;
+    auto mark = [&](int i) -> int {
+      if (!ev) return 0;
+      EventRecordFn rec = event_record_fn();
+      if (!rec) return (int)cudaErrorInitializationError;
+      return rec((CUevent)ev[i], (CUstream)stream) == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidResourceHandle;
+    };
+    int rc = mark(0);
+    if (!rc) rc = k2b_norm_quant(x, P[K2B_SLOT_PRENORM], ps, ph, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+    if (!rc) rc = mark(1);
     if (!rc)
       rc = k2b_qkv(w.xq, w.xs, P[K2B_SLOT_WQ], P[K2B_SLOT_SQ], P[K2B_SLOT_WK], P[K2B_SLOT_SK], P[K2B_SLOT_WV],
                    P[K2B_SLOT_SV], nullptr, nullptr, P[K2B_SLOT_QNORM], P[K2B_SLOT_KNORM], freqs, w.q, w.k, w.v,
                    nullptr, m, length, heads * 128, kvheads * 128, hidden, qk_eps, qk_eps, stream);
+    if (!rc) rc = mark(2);
     if (!rc)
       rc = k2b_attention_quant(w.q, w.k, w.v, w.oq, w.os, batch, heads, kvheads, length, length, 128,
                                (long long)length * qst, 128, qst, (long long)length * kst, 128, kst,
                                (long long)length * kst, 128, kst, stream);
+    if (!rc) rc = mark(3);
     if (!rc)
       rc = k2b_gated_residual(w.oq, w.os, P[K2B_SLOT_WO], P[K2B_SLOT_SO], pg, x, w.x1, m, length, hidden,
                               heads * 128, stream);
+    if (!rc) rc = mark(4);
     if (!rc)
       rc = k2b_norm_quant(w.x1, P[K2B_SLOT_POSTNORM], ss, sh, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+    if (!rc) rc = mark(5);
     if (!rc)
       rc = k2b_swiglu_quant(w.xq, w.xs, P[K2B_SLOT_WG], P[K2B_SLOT_SG], P[K2B_SLOT_WU], P[K2B_SLOT_SU], w.hq, w.hs, m,
                             mlp, hidden, stream);
+    if (!rc) rc = mark(6);
     if (!rc)
       rc = k2b_gated_residual(w.hq, w.hs, P[K2B_SLOT_WD], P[K2B_SLOT_SD], sg, w.x1, x, m, length, hidden, mlp,
                               stream);
+    if (!rc) rc = mark(7);
     if (rc) return rc;
   }
   return 0;

@@ -143,17 +143,23 @@ class Krea2Blocks:
         check(0 if nbytes > 0 else 1, "k2b_block_workspace_bytes")
         self.workspace = torch.empty(int(nbytes), dtype=torch.uint8, device=device)
 
-    def forward_(self, x: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-        """In-place forward of the residual stream x bf16 [batch*length, hidden]."""
+    def forward_(self, x: torch.Tensor, freqs: torch.Tensor, events=None) -> torch.Tensor:
+        """In-place forward of the residual stream x bf16 [batch*length, hidden].
+        events: optional list of nblocks*8 torch.cuda.Event (enable_timing)
+        recorded between the native launches (see k2b_forward_blocks)."""
         cfg = self.cfg
         ops._cuda(x, freqs)
         ops._need(x.dtype == torch.bfloat16 and tuple(x.shape) == (self.batch * self.length, cfg.hidden),
                   "forward: x shape")
         ops._need(freqs.dtype == torch.float32 and freqs.numel() == self.length * 256, "forward: freqs shape")
+        ev = None
+        if events is not None:
+            ops._need(len(events) == 8 * len(self.blocks), "forward: need 8 events per block")
+            ev = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
         check(lib().k2b_forward_blocks(self._table, len(self.blocks), ops._p(x), ops._p(freqs),
                                        ops._p(self.workspace), self.workspace.numel(), self.batch, self.length,
                                        cfg.hidden, cfg.heads, cfg.kvheads, cfg.mlp, ctypes.c_float(cfg.eps),
-                                       ctypes.c_float(cfg.qk_eps), ops._stream()), "k2b_forward_blocks")
+                                       ctypes.c_float(cfg.qk_eps), ev, ops._stream()), "k2b_forward_blocks")
         return x
 
 

@@ -140,12 +140,15 @@ int k2b_attention_quant(const void* q, const void* k, const void* v, void* oq, v
  *   18 modulation bf16 [6, batch, hidden] = (ps, ph, pg, ss, sh, sg)
  * (W = prepared int8, S = prepared fp32 scales).  x bf16 [batch*length,
  * hidden] is updated in place; freqs fp32 [length,64,2,2];
- * workspace >= k2b_block_workspace_bytes(). hidden == heads*128. */
+ * workspace >= k2b_block_workspace_bytes(). hidden == heads*128.
+ * events (nullable): nblocks*8 cudaEvent_t; events[8b+i] is recorded on the
+ * stream before launch i of block b (0 norm_quant, 1 qkv, 2 attention,
+ * 3 out-proj, 4 norm_quant, 5 gate/up, 6 down) and events[8b+7] after it. */
 int k2b_block_slots(void);
 long long k2b_block_workspace_bytes(int rows, int hidden, int heads, int kvheads, int mlp);
 int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, const void* freqs, void* workspace,
                        long long workspace_bytes, int batch, int length, int hidden, int heads, int kvheads, int mlp,
-                       float eps, float qk_eps, void* stream);
+                       float eps, float qk_eps, void* const* events, void* stream);
 
 /* -------------------------------------- reference-named exports (shims) --
  * Same names and argument order as the reference's kernel libraries so that

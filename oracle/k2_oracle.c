@@ -258,34 +258,41 @@ static void unpack_row(const uint8_t* p, int8_t* out, int K) {
     }
 }
 
+/* Unpacks packed INT4 rows [n, K/2] (+ fp16 scales [n, K/128]) into int8
+ * codes [n, K] and fp32 scales [n, K/128]. */
+int k2o_unpack_weight(const uint8_t* W, const uint16_t* sW, int n, int K, int8_t* wu, float* swf) {
+    if (K % 128) return 1;
+    int G = K / 128;
+    for (int c = 0; c < n; ++c) {
+        unpack_row(W + (int64_t)c * (K / 2), wu + (int64_t)c * K, K);
+        for (int g = 0; g < G; ++g) swf[(int64_t)c * G + g] = k2o_f16_to_f32(sW[(int64_t)c * G + g]);
+    }
+    return 0;
+}
+
 /*
- * Group-scaled W4A4 GEMM, fp32 result p[r,c] for the selected rows.
+ * Group-scaled W4A4 GEMM, fp32 result p[r,c] for the selected rows and the
+ * output columns [c0, c1).
  * Accumulation: int32 per (row, 128-wide K group) as the s4 mma of
  * kernels/joint_projection.cu:51-56 produces; dequant of the contract
  * (group-128 scales on both operands; the reference's per-row/per-channel
  * version is T(float(acc)*xs*ws), kernels/joint_projection.cu:57-59):
  *     p = 0;  for g:  u = fp32(float(acc_g) * sA[r,g]);  p = fmaf(u, sW[c,g], p)
- * A u8 [M,K/2] + fp16 [M,K/128]; W u8 [N,K/2] + fp16 [N,K/128].
- * rows == NULL selects rows 0..nrows-1.  out fp32 [nrows, N].
- * acc_out (optional) receives the int32 accumulators [nrows, N, K/128].
+ * A u8 [M,K/2] + fp16 [M,K/128]; W given unpacked (k2o_unpack_weight).
+ * rows == NULL selects rows 0..nrows-1.  out fp32 [nrows, ldo] (column c at
+ * out[i*ldo + c]); acc_out (optional) int32 [nrows, N, K/128].
  */
-int k2o_gemm_w4a4(const uint8_t* A, const uint16_t* sA, const uint8_t* W, const uint16_t* sW,
-                  int M, int N, int K, const int* rows, int nrows, float* out, int32_t* acc_out) {
-    if (K % 128 || M <= 0 || N <= 0) return 1;
+int k2o_gemm_w4a4_cols(const uint8_t* A, const uint16_t* sA, const int8_t* wu, const float* swf, int M, int N,
+                       int K, const int* rows, int nrows, int c0, int c1, float* out, int ldo, int32_t* acc_out) {
+    if (K % 128 || M <= 0 || N <= 0 || c0 < 0 || c1 > N) return 1;
     int G = K / 128;
-    int8_t* wu = (int8_t*)malloc((size_t)N * K);
-    float* swf = (float*)malloc(sizeof(float) * (size_t)N * G);
-    for (int c = 0; c < N; ++c) {
-        unpack_row(W + (int64_t)c * (K / 2), wu + (int64_t)c * K, K);
-        for (int g = 0; g < G; ++g) swf[(int64_t)c * G + g] = k2o_f16_to_f32(sW[(int64_t)c * G + g]);
-    }
+    int8_t* au = (int8_t*)malloc((size_t)K);
+    float* saf = (float*)malloc(sizeof(float) * (size_t)G);
     for (int i = 0; i < nrows; ++i) {
         int r = rows ? rows[i] : i;
-        int8_t* au = (int8_t*)malloc((size_t)K);
-        float* saf = (float*)malloc(sizeof(float) * (size_t)G);
         unpack_row(A + (int64_t)r * (K / 2), au, K);
         for (int g = 0; g < G; ++g) saf[g] = k2o_f16_to_f32(sA[(int64_t)r * G + g]);
-        for (int c = 0; c < N; ++c) {
+        for (int c = c0; c < c1; ++c) {
             const int8_t* wr = wu + (int64_t)c * K;
             float p = 0.0f;
             for (int g = 0; g < G; ++g) {
@@ -295,13 +302,11 @@ int k2o_gemm_w4a4(const uint8_t* A, const uint16_t* sA, const uint8_t* W, const 
                 float u = (float)acc * saf[g];
                 p = fmaf(u, swf[(int64_t)c * G + g], p);
             }
-            out[(int64_t)i * N + c] = p;
+            out[(int64_t)i * ldo + c] = p;
         }
-        free(au);
-        free(saf);
     }
-    free(wu);
-    free(swf);
+    free(au);
+    free(saf);
     return 0;
 }
 

@@ -64,7 +64,8 @@ def _declare(L):
     L.k2o_norm_quant.argtypes = [P, P, P, P, P, P, I, I, I, I, I, F]
     L.k2o_rotate_quant.argtypes = [P, P, P, I, I]
     L.k2o_norm_mod.argtypes = [P, P, P, P, P, I, I, I, I, I, F]
-    L.k2o_gemm_w4a4.argtypes = [P, P, P, P, I, I, I, P, I, P, P]
+    L.k2o_unpack_weight.argtypes = [P, P, I, I, P, P]
+    L.k2o_gemm_w4a4_cols.argtypes = [P, P, P, P, I, I, I, P, I, I, I, P, I, P]
     L.k2o_qk_norm_rope.argtypes = [P, I, I, I, P, F, P, I, P, P]
     L.k2o_gated_residual.argtypes = [P, I, I, P, P, I, P, P]
     L.k2o_swiglu_quant.argtypes = [P, P, I, I, P, P, P]
@@ -194,31 +195,54 @@ def rotate_quant(x):
     return q, s
 
 
-def gemm_w4a4(A, sA, W, sW, rows=None, with_acc=False):
-    """Group-scaled W4A4 GEMM.  A u8 [M,K/2], sA fp16 bits [M,K/128], W u8
-    [N,K/2], sW fp16 bits [N,K/128].  rows: optional row indices.
-    Returns fp32 [len(rows), N] (and int32 [len(rows), N, K/128])."""
-    A = _c(A, np.uint8)
+def unpack_weight(W, sW):
+    """Packed INT4 [N,K/2] + fp16 bits [N,K/128] -> (int8 [N,K], fp32 [N,K/128])."""
     W = _c(W, np.uint8)
-    sA = _c(sA, np.uint16)
     sW = _c(sW, np.uint16)
+    N, K2 = W.shape
+    K = 2 * K2
+    wu = np.empty((N, K), np.int8)
+    swf = np.empty((N, K // 128), np.float32)
+    L = lib()
+
+    def job(ab):
+        a, b = ab
+        assert L.k2o_unpack_weight(_p(W[a:b]), _p(sW[a:b]), b - a, K, _p(wu[a:b]), _p(swf[a:b])) == 0
+
+    with ThreadPoolExecutor(_workers()) as ex:
+        list(ex.map(job, _row_blocks(N, _workers() * 2)))
+    return wu, swf
+
+
+def gemm_w4a4(A, sA, W, sW, rows=None, with_acc=False, unpacked=None):
+    """Group-scaled W4A4 GEMM.  A u8 [M,K/2], sA fp16 bits [M,K/128], W u8
+    [N,K/2], sW fp16 bits [N,K/128] (or unpacked=(int8 [N,K], fp32 [N,K/128])).
+    rows: optional row indices.  Returns fp32 [len(rows), N] (and int32
+    [len(rows), N, K/128])."""
+    A = _c(A, np.uint8)
+    sA = _c(sA, np.uint16)
+    wu, swf = unpacked if unpacked is not None else unpack_weight(W, sW)
     M, K2 = A.shape
-    N = W.shape[0]
+    N = wu.shape[0]
     K = K2 * 2
     rows = np.arange(M, dtype=np.int32) if rows is None else _c(rows, np.int32)
     n = rows.size
     out = np.empty((n, N), np.float32)
     acc = np.empty((n, N, K // 128), np.int32) if with_acc else None
     L = lib()
+    w = _workers()
+    rb = _row_blocks(n, w)
+    cb = _row_blocks(N, max(1, (2 * w) // len(rb)))
+    jobs = [(a, b, c0, c1) for a, b in rb for c0, c1 in cb]
 
-    def job(ab):
-        a, b = ab
-        code = L.k2o_gemm_w4a4(_p(A), _p(sA), _p(W), _p(sW), M, N, K, _p(rows[a:b]), b - a,
-                               _p(out[a:b]), _p(acc[a:b]) if with_acc else None)
+    def job(t):
+        a, b, c0, c1 = t
+        code = L.k2o_gemm_w4a4_cols(_p(A), _p(sA), _p(wu), _p(swf), M, N, K, _p(rows[a:b]), b - a, c0, c1,
+                                    _p(out[a:b]), N, _p(acc[a:b]) if with_acc else None)
         assert code == 0
 
-    with ThreadPoolExecutor(_workers()) as ex:
-        list(ex.map(job, _row_blocks(n, _workers())))
+    with ThreadPoolExecutor(w) as ex:
+        list(ex.map(job, jobs))
     return (out, acc) if with_acc else out
 
 
