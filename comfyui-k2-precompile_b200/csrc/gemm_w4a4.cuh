@@ -8,22 +8,26 @@
 // (kernels/qk_norm_rope.cu:19-133).
 //
 // Tile: 128 rows (M) x 256 columns (N) per CTA, K consumed one 128-wide
-// quantisation group per pipeline stage.  Roles (384 threads):
+// quantisation group per pipeline stage.  Roles (640 threads):
 //   warp 0      TMA producer: packed A group tile (128 x 64 B), prepared W
 //               group tile (256 x 128 B, 128B-swizzled), W group scales (1 KB)
 //   warp 1      TMEM allocator + single-thread MMA issuer (4 x K=32 MMAs per group)
 //   warps 2-3   A unpackers: s4 -> s8 (x16) into the 128B-swizzled UMMA layout
-//   warps 4-11  epilogue: TMEM lane quadrant = warp % 4, column half = (warp-4)/4
+//   warps 4-19  epilogue: TMEM lane quadrant = warp % 4, column quarter
+//               = (warp-4)/4 (64 columns of one row per thread)
 // TMEM: 2 x 256 int32 columns, one per group in flight (ping-pong), so the MMA
 // of group g+1 overlaps the dequant of group g.  The fp32 group sum lives in
-// the epilogue registers (128 per thread).
+// the epilogue registers (64 per thread); four epilogue warps per scheduler
+// hide the TMEM load latency.  setmaxnreg gives the TMA/MMA/unpack warpgroup
+// 32 registers and the four epilogue warpgroups 112.
 //
 // Dequant contract (oracle: k2o_gemm_w4a4):
 //   p = 0;  for g:  u = fp32(acc_g * sA[r,g]);  p = fmaf(u, sW[c,g], p)
 // The s8 operands carry 16x the INT4 codes (the nibble is kept in the high
-// half of each byte), so the TMEM accumulator is 256*acc_g (|.| <= 2^21).
-// It is turned into fp32 with the exponent-bias trick (bits + 0x4B400000 ->
-// 12582912 + x exactly) and the bias is removed inside the first fma:
+// half of each byte), so the TMEM accumulator is x = 256*acc_g (|x| <= 2^21).
+// The epilogue turns it into fp32 with an integer add of the exponent bias
+// (bits 0x4B400000 + x read as the float 12582912 + x, exactly) and removes
+// the bias inside the first fma:
 //   u = fma(12582912 + x, sA/256, -12582912*sA/256) = fp32(acc_g * sA)
 // (both sA/256 and 12582912*sA/256 are exact for an fp16-valued sA).
 #pragma once
@@ -35,7 +39,13 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
 constexpr int GEMM_STAGES = 3;   // prepared W + unpacked A
 constexpr int GEMM_PSTAGES = 4;  // packed A and W scales
-constexpr int GEMM_THREADS = 384;
+constexpr int GEMM_EPI_WARPS = 16;
+constexpr int GEMM_THREADS = 128 + 32 * GEMM_EPI_WARPS;  // 640
+// Registers per thread the kernel is compiled with (65536 / 640 rounded down
+// to the allocation granule).  Warpgroup 0 drops to 32 and the epilogue
+// warpgroups grow to 112 (128*32 + 512*112 == 640*96); the launcher refuses
+// any other allocation.
+constexpr int GEMM_LAUNCH_REGS = 96;
 
 constexpr int GEMM_W_BYTES = GEMM_BN * 128;       // 32 KB
 constexpr int GEMM_UA_BYTES = GEMM_BM * 128;      // 16 KB
@@ -48,8 +58,8 @@ constexpr int GEMM_OFF_SC = GEMM_OFF_PA + GEMM_PSTAGES * GEMM_PA_BYTES;
 constexpr int GEMM_OFF_BAR = GEMM_OFF_SC + GEMM_PSTAGES * GEMM_SC_BYTES;
 constexpr int GEMM_NBARS = 3 * GEMM_STAGES + 4 * GEMM_PSTAGES + 4;
 constexpr int GEMM_SMEM_BYTES = GEMM_OFF_BAR + GEMM_NBARS * 8 + 16 + 1024;  // + alignment slack
-// The SwiGLU exchange buffer reuses the W stages after the main loop.
-constexpr int GEMM_XCH_STRIDE = 272;  // bytes per row: 128 bf16 + 16 B pad
+// Accumulator seed: as fp32 bits, 0x4B400000 + x reads as 12582912 + x for |x| < 2^22.
+constexpr uint32_t kAccBias = 0x4B400000u;
 
 enum SegKind : int {
   SEG_BF16 = 0,       // bf16(p)
@@ -96,6 +106,35 @@ __device__ __forceinline__ void unpack_chunk(uint4 v, uint4& lo, uint4& hi) {
   lo.w = (v.w << 4) & 0xF0F0F0F0u; hi.w = v.w & 0xF0F0F0F0u;
 }
 
+// Sylvester H128 stages h = 1..32 on 64 consecutive values held by one thread.
+__device__ __forceinline__ void hadamard64_regs(float (&v)[64]) {
+#pragma unroll
+  for (int lh = 0; lh < 6; ++lh) {
+    const int h = 1 << lh;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int lo = ((i >> lh) << (lh + 1)) | (i & (h - 1));
+      const float a = v[lo], b = v[lo + h];
+      v[lo] = __fadd_rn(a, b);
+      v[lo + h] = __fsub_rn(a, b);
+    }
+  }
+}
+
+// Named barrier over the 16 epilogue warps only.
+__device__ __forceinline__ void epi_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * GEMM_EPI_WARPS) : "memory");
+}
+
+__device__ __forceinline__ void store_bf16x64(__nv_bfloat16* o, const float (&v)[64]) {
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    uint4 w4 = make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                          pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+    *reinterpret_cast<uint4*>(o + i) = w4;
+  }
+}
+
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w4a4_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ WeightMaps wmaps,
                      const __grid_constant__ GemmParams p) {
@@ -109,8 +148,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* empty_pa = full_pa + GEMM_PSTAGES;      // [PSTAGES] unpackers done
   uint64_t* full_sc = empty_pa + GEMM_PSTAGES;      // [PSTAGES] W scales landed
   uint64_t* empty_sc = full_sc + GEMM_PSTAGES;      // [PSTAGES] epilogue done with scales
-  uint64_t* tmem_full = empty_sc + GEMM_PSTAGES;    // [2]
-  uint64_t* tmem_empty = tmem_full + 2;             // [2]
+  uint64_t* tmem_full = empty_sc + GEMM_PSTAGES;    // [2] MMAs of a group done
+  uint64_t* tmem_empty = tmem_full + 2;             // [2] buffer drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + GEMM_NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -138,11 +177,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full_pa[i], 1);
       mbar_init(&empty_pa[i], 2);
       mbar_init(&full_sc[i], 1);
-      mbar_init(&empty_sc[i], 8);
+      mbar_init(&empty_sc[i], GEMM_EPI_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tmem_full[i], 1);
-      mbar_init(&tmem_empty[i], 8);
+      mbar_init(&tmem_empty[i], GEMM_EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -157,208 +196,185 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   int issued_w = 0, issued_pa = 0, issued_sc = 0, issued_mma = 0;
-  if (warp == 0) {
-    // ------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      const CUtensorMap* wmap = &wmaps.m[pairw ? 0 : seg];
+  if (warp < 4) {
+    setmaxnreg_dec32();
+    if (warp == 0) {
+      // ----------------------------------------------------- TMA producer
+      if (lane == 0) {
+        const CUtensorMap* wmap = &wmaps.m[pairw ? 0 : seg];
+        for (int g = 0; g < G; ++g) {
+          const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
+          const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
+          if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full_w[s], GEMM_W_BYTES);
+          if (pairw) {
+            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, &wmaps.m[0], &full_w[s], g * 128, n0);
+            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES + GEMM_W_BYTES / 2, &wmaps.m[1], &full_w[s], g * 128,
+                        n0);
+          } else {
+            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_w[s], g * 128, n0);
+          }
+          issued_w = g + 1;
+          if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pa[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
+          tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
+          issued_pa = g + 1;
+          if (g >= GEMM_PSTAGES && !mbar_wait(&empty_sc[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full_sc[ps], GEMM_SC_BYTES);
+          if (pairw) {
+            bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES, S.wscale + (int64_t)g * S.n + n0, GEMM_SC_BYTES / 2,
+                      &full_sc[ps]);
+            bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES + GEMM_SC_BYTES / 2, S.wscale2 + (int64_t)g * S.n + n0,
+                      GEMM_SC_BYTES / 2, &full_sc[ps]);
+          } else {
+            bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES, S.wscale + (int64_t)g * S.n + n0, GEMM_SC_BYTES,
+                      &full_sc[ps]);
+          }
+          issued_sc = g + 1;
+        }
+      }
+    } else if (warp == 1) {
+      // ----------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc = make_idesc(2, 1, 1, 0, 0, GEMM_BM, GEMM_BN);
+        for (int g = 0; g < G; ++g) {
+          const int s = g % GEMM_STAGES, b = g & 1;
+          const uint32_t ph = (g / GEMM_STAGES) & 1, bph = (g >> 1) & 1;
+          if (!mbar_wait(&full_w[s], ph, abort_flag, ERR_WAIT_MMA)) break;
+          if (!mbar_wait(&full_ua[s], ph, abort_flag, ERR_WAIT_MMA)) break;
+          if (g >= 2 && !mbar_wait(&tmem_empty[b], bph ^ 1, abort_flag, ERR_WAIT_MMA)) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES);
+          const uint32_t w_base = smem_u32(smem + GEMM_OFF_W + s * GEMM_W_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = umma_desc_sw128(a_base + 32 * k, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(w_base + 32 * k, 16, 1024);
+            mma_i8_ss(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
+          }
+          mma_commit(&empty_s[s]);
+          mma_commit(&tmem_full[b]);
+          issued_mma = g + 1;
+        }
+      }
+    } else {
+      // ----------------------------------------------------- A unpackers
+      const int t = threadIdx.x - 64;  // 0..63
       for (int g = 0; g < G; ++g) {
         const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
         const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
-        if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full_w[s], GEMM_W_BYTES);
-        if (pairw) {
-          tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, &wmaps.m[0], &full_w[s], g * 128, n0);
-          tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES + GEMM_W_BYTES / 2, &wmaps.m[1], &full_w[s], g * 128, n0);
-        } else {
-          tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_w[s], g * 128, n0);
-        }
-        issued_w = g + 1;
-        if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pa[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
-        tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
-        issued_pa = g + 1;
-        if (g >= GEMM_PSTAGES && !mbar_wait(&empty_sc[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full_sc[ps], GEMM_SC_BYTES);
-        if (pairw) {
-          bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES, S.wscale + (int64_t)g * S.n + n0, GEMM_SC_BYTES / 2,
-                    &full_sc[ps]);
-          bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES + GEMM_SC_BYTES / 2, S.wscale2 + (int64_t)g * S.n + n0,
-                    GEMM_SC_BYTES / 2, &full_sc[ps]);
-        } else {
-          bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES, S.wscale + (int64_t)g * S.n + n0, GEMM_SC_BYTES,
-                    &full_sc[ps]);
-        }
-        issued_sc = g + 1;
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(2, 1, 1, 0, 0, GEMM_BM, GEMM_BN);
-      for (int g = 0; g < G; ++g) {
-        const int s = g % GEMM_STAGES, b = g & 1;
-        const uint32_t ph = (g / GEMM_STAGES) & 1, bph = (g >> 1) & 1;
-        if (!mbar_wait(&full_w[s], ph, abort_flag, ERR_WAIT_MMA)) break;
-        if (!mbar_wait(&full_ua[s], ph, abort_flag, ERR_WAIT_MMA)) break;
-        if (g >= 2 && !mbar_wait(&tmem_empty[b], bph ^ 1, abort_flag, ERR_WAIT_MMA)) break;
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES);
-        const uint32_t w_base = smem_u32(smem + GEMM_OFF_W + s * GEMM_W_BYTES);
+        if (!mbar_wait(&full_pa[ps], pph, abort_flag, ERR_WAIT_UNPACK)) break;
+        if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_UNPACK)) break;
+        const uint4* src = reinterpret_cast<const uint4*>(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES);
+        uint8_t* dst = smem + GEMM_OFF_UA + s * GEMM_UA_BYTES;
+        // 16-byte chunk i = t + 64*it: row i/4 (= t/4 + 16*it), K columns 32*(i%4) .. +31
+        const int c = t & 3, r0 = t >> 2;  // (r0 + 16*it) & 7 == r0 & 7
+        uint8_t* d0 = dst + r0 * 128 + (((2 * c) ^ (r0 & 7)) << 4);
+        uint8_t* d1 = dst + r0 * 128 + (((2 * c + 1) ^ (r0 & 7)) << 4);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = umma_desc_sw128(a_base + 32 * k, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(w_base + 32 * k, 16, 1024);
-          mma_i8_ss(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
-        }
-        mma_commit(&empty_s[s]);
-        mma_commit(&tmem_full[b]);
-        issued_mma = g + 1;
-      }
-    }
-  } else if (warp < 4) {
-    // ------------------------------------------------------- A unpackers
-    const int t = threadIdx.x - 64;  // 0..63
-    for (int g = 0; g < G; ++g) {
-      const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
-      const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
-      if (!mbar_wait(&full_pa[ps], pph, abort_flag, ERR_WAIT_UNPACK)) break;
-      if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_UNPACK)) break;
-      const uint4* src = reinterpret_cast<const uint4*>(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES);
-      uint8_t* dst = smem + GEMM_OFF_UA + s * GEMM_UA_BYTES;
+        for (int half = 0; half < 2; ++half) {
+          uint4 pk[4];
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int i = t + 64 * it;  // 16-byte chunk: row i/4, K columns 32*(i%4) .. +31
-        const int r = i >> 2, c = i & 3;
-        uint4 lo, hi;
-        unpack_chunk(src[i], lo, hi);
-        *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&empty_pa[ps]);
-        mbar_arrive(&full_ua[s]);
+          for (int it = 0; it < 4; ++it) pk[it] = src[t + 64 * (4 * half + it)];
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            uint4 lo, hi;
+            unpack_chunk(pk[it], lo, hi);
+            *reinterpret_cast<uint4*>(d0 + (4 * half + it) * 16 * 128) = lo;
+            *reinterpret_cast<uint4*>(d1 + (4 * half + it) * 16 * 128) = hi;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty_pa[ps]);
+          mbar_arrive(&full_ua[s]);
+        }
       }
     }
   } else {
     // ------------------------------------------------------- epilogue
+    setmaxnreg_inc112();
     const int q = warp & 3;
-    const int half = (warp - 4) >> 2;
+    const int cq = (warp - 4) >> 2;  // column quarter 0..3
     const int rloc = 32 * q + lane;
     const int row = m0 + rloc;
     const bool row_ok = row < p.M;
     const __half* sa_row = p.sa + (int64_t)(row_ok ? row : 0) * G;
-    float acc[128];
-#pragma unroll
-    for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + cq * 64;
     bool ok = true;
+    float2 acc2[32];  // columns (2j, 2j+1)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc2[j] = make_float2(0.0f, 0.0f);
+    __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
     for (int g = 0; g < G && ok; ++g) {
       const int b = g & 1, ps = g % GEMM_PSTAGES;
       const uint32_t bph = (g >> 1) & 1, pph = (g / GEMM_PSTAGES) & 1;
-      const float sa = row_ok ? __fmul_rn(__half2float(sa_row[g]), 0.00390625f) : 0.0f;
+      const float sa = row_ok ? __fmul_rn(__half2float(sa_next), 0.00390625f) : 0.0f;
+      if (g + 1 < G) sa_next = sa_row[g + 1];
       const float sbias = __fmul_rn(sa, -12582912.0f);
+      const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sbias, sbias);
       if (!mbar_wait(&full_sc[ps], pph, abort_flag, ERR_WAIT_EPILOGUE)) { ok = false; break; }
       if (!mbar_wait(&tmem_full[b], bph, abort_flag, ERR_WAIT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
-      const float* scs = reinterpret_cast<const float*>(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES) + half * 128;
-      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + b * GEMM_BN + half * 128;
-      uint32_t buf[2][16];
-      tmem_ld16(taddr, buf[0]);
-      tmem_wait_ld_regs(buf[0]);
+      const float4* scs = reinterpret_cast<const float4*>(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES + cq * 64 * 4);
+      const uint32_t taddr = lane_base + b * GEMM_BN;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        if (c + 1 < 8) tmem_ld16(taddr + 16 * (c + 1), buf[(c + 1) & 1]);
-        if (c + 1 == 8) {
-          // every column of this buffer is in registers: hand it back to the MMA
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[16];
+        tmem_ld16(taddr + 16 * c, v);
+        tmem_wait_ld_regs(v);
+        if (c == 3) {
+          // every column is in registers: hand the buffer back to the MMA
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[b]);
         }
-        const uint32_t* v = buf[c & 1];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float4 sw4 = *reinterpret_cast<const float4*>(scs + 16 * c + (i & ~3));
-          const float swa = (i & 2) ? sw4.z : sw4.x, swb = (i & 2) ? sw4.w : sw4.y;
-          const float2 fb = make_float2(__int_as_float((int)(v[i] + 0x4B400000u)),
-                                        __int_as_float((int)(v[i + 1] + 0x4B400000u)));
-          const float2 u = ffma2(fb, make_float2(sa, sa), make_float2(sbias, sbias));
-          const float2 r = ffma2(u, make_float2(swa, swb), make_float2(acc[16 * c + i], acc[16 * c + i + 1]));
-          acc[16 * c + i] = r.x;
-          acc[16 * c + i + 1] = r.y;
+        for (int i = 0; i < 16; i += 4) {
+          const float4 sw = scs[(16 * c + i) / 4];  // scales of columns 16c+i .. +3
+          const float2 u0 = __ffma2_rn(
+              make_float2(__uint_as_float(v[i] + kAccBias), __uint_as_float(v[i + 1] + kAccBias)), sa2, sb2);
+          const float2 u1 = __ffma2_rn(
+              make_float2(__uint_as_float(v[i + 2] + kAccBias), __uint_as_float(v[i + 3] + kAccBias)), sa2, sb2);
+          acc2[(16 * c + i) / 2] = __ffma2_rn(u0, make_float2(sw.x, sw.y), acc2[(16 * c + i) / 2]);
+          acc2[(16 * c + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(16 * c + i) / 2 + 1]);
         }
-        if (c + 1 < 8) tmem_wait_ld_regs(buf[(c + 1) & 1]);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_sc[ps]);
     }
 
+    float acc[64];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      acc[2 * j] = acc2[j].x;
+      acc[2 * j + 1] = acc2[j].y;
+    }
+
     // ---------------------------------------------------- final epilogue
     // CTA-uniform decision: every epilogue warp reaches this barrier, then all
-    // of them see the same abort flag (the SwiGLU path has a second barrier).
-    asm volatile("bar.sync 2, 256;" ::: "memory");
+    // of them see the same abort flag (the pair-exchanging paths have more).
+    epi_barrier();
     ok = ok && (*abort_flag == 0);
+    // Exchange space: the W stages are idle once every MMA has completed.
+    float* xch = reinterpret_cast<float*>(smem + GEMM_OFF_W);
     if (ok) {
-      const int col0 = n0 + half * 128;  // first column (within the segment) of this thread
+      const int col0 = n0 + cq * 64;  // first segment column of this thread (non-SwiGLU kinds)
       if (S.kind == SEG_F32) {
         if (row_ok) {
           float* o = reinterpret_cast<float*>(S.out) + (int64_t)row * S.ld + col0;
 #pragma unroll
-          for (int i = 0; i < 128; i += 4)
+          for (int i = 0; i < 64; i += 4)
             *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
         }
       } else if (S.kind == SEG_BF16 || S.kind == SEG_SIGMOID) {
         if (row_ok) {
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + col0;
+          if (S.kind == SEG_SIGMOID) {
 #pragma unroll
-          for (int i = 0; i < 128; i += 8) {
-            float t[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              t[j] = acc[i + j];
-              if (S.kind == SEG_SIGMOID) t[j] = sigmoid_contract(bf16_round(t[j]));
-            }
-            uint4 w4 = make_uint4(pack_bf16x2(t[0], t[1]), pack_bf16x2(t[2], t[3]), pack_bf16x2(t[4], t[5]),
-                                  pack_bf16x2(t[6], t[7]));
-            *reinterpret_cast<uint4*>(o + i) = w4;
+            for (int i = 0; i < 64; ++i) acc[i] = sigmoid_contract(bf16_round(acc[i]));
           }
-        }
-      } else if (S.kind == SEG_QKNORM) {
-        if (row_ok) {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) acc[i] = bf16_round(acc[i]);
-          // reduction order of kernels/joint_projection.cu:141-146
-          float part[32];
-#pragma unroll
-          for (int l = 0; l < 32; ++l) {
-            float s2 = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s2 = __fmaf_rn(acc[4 * l + j], acc[4 * l + j], s2);
-            part[l] = s2;
-          }
-#pragma unroll
-          for (int off = 16; off; off >>= 1)
-#pragma unroll
-            for (int l = 0; l < off; ++l) part[l] = __fadd_rn(part[l], part[l + off]);
-          const float inv = __frsqrt_rn(__fadd_rn(__fmul_rn(part[0], 0.0078125f), S.eps));
-          const int token = row % p.length;
-          const float* f = p.freqs + (int64_t)token * 256;
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + col0;
-#pragma unroll
-          for (int i = 0; i < 128; i += 8) {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              const int c = i + j;
-              const float a = bf16_round(__fmul_rn(__fmul_rn(acc[c], inv), __fadd_rn(S.normw[c], 1.0f)));
-              const float bb = bf16_round(__fmul_rn(__fmul_rn(acc[c + 1], inv), __fadd_rn(S.normw[c + 1], 1.0f)));
-              const float4 fr = __ldg(reinterpret_cast<const float4*>(f + 2 * c));
-              const float o0 = __fmaf_rn(fr.x, a, __fmul_rn(fr.y, bb));
-              const float o1 = __fmaf_rn(fr.z, a, __fmul_rn(fr.w, bb));
-              w[j / 2] = pack_bf16x2(o0, o1);
-            }
-            *reinterpret_cast<uint4*>(o + i) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
+          store_bf16x64(reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + col0, acc);
         }
       } else if (S.kind == SEG_RESIDUAL) {
         if (row_ok) {
@@ -367,7 +383,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const __nv_bfloat16* rs = p.resid + (int64_t)row * S.ld + col0;
           __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + col0;
 #pragma unroll
-          for (int i = 0; i < 128; i += 8) {
+          for (int i = 0; i < 64; i += 8) {
             const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(gt + i));
             const uint4 r4 = __ldg(reinterpret_cast<const uint4*>(rs + i));
             const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g4);
@@ -383,72 +399,131 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             *reinterpret_cast<uint4*>(o + i) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-      } else if (pairw) {
-        // Column half 0 holds the gate projection and half 1 the up projection
-        // of the same 128 output columns; half 1 hands bf16(up) over in smem.
-        uint8_t* xch = smem + GEMM_OFF_W;  // W stages are idle once every MMA has completed
-        if (half == 1) {
-          uint8_t* dst = xch + rloc * GEMM_XCH_STRIDE;
+      } else if (S.kind == SEG_QKNORM) {
+        // A head (128 columns) spans the warp pair (cq even: columns 0-63,
+        // cq odd: 64-127).  Reduction order of kernels/joint_projection.cu:141-146:
+        // lane l of the reference holds columns 4l..4l+3, then a shfl_down tree.
 #pragma unroll
-          for (int i = 0; i < 128; i += 8) {
-            uint4 w4 = make_uint4(pack_bf16x2(acc[i], acc[i + 1]), pack_bf16x2(acc[i + 2], acc[i + 3]),
-                                  pack_bf16x2(acc[i + 4], acc[i + 5]), pack_bf16x2(acc[i + 6], acc[i + 7]));
-            *reinterpret_cast<uint4*>(dst + 2 * i) = w4;
-          }
+        for (int i = 0; i < 64; ++i) acc[i] = bf16_round(acc[i]);
+        float part[16];
+#pragma unroll
+        for (int l = 0; l < 16; ++l) {
+          float s2 = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) s2 = __fmaf_rn(acc[4 * l + j], acc[4 * l + j], s2);
+          part[l] = s2;
         }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (half == 0 && row_ok) {
-          const uint8_t* src = xch + rloc * GEMM_XCH_STRIDE;
+        float* pbuf = xch + ((cq >> 1) * 128 + rloc) * 17;  // per (head, row): 16 partials + inv
+        if (cq & 1) {
 #pragma unroll
-          for (int i = 0; i < 128; i += 8) {
-            const uint4 u4 = *reinterpret_cast<const uint4*>(src + 2 * i);
-            const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&u4);
+          for (int l = 0; l < 16; ++l) pbuf[l] = part[l];
+        }
+        epi_barrier();
+        if (!(cq & 1)) {
+          // tree step 16: reference lane l (< 16) adds lane l + 16 (the odd warp's partial l)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 uf = __bfloat1622float2(u2[j]);
-              const float g0 = bf16_round(acc[i + 2 * j]), g1 = bf16_round(acc[i + 2 * j + 1]);
-              const float a0 = bf16_round(silu_contract(g0)), a1 = bf16_round(silu_contract(g1));
-              acc[i + 2 * j] = bf16_round(__fmul_rn(a0, uf.x));
-              acc[i + 2 * j + 1] = bf16_round(__fmul_rn(a1, uf.y));
-            }
-          }
-          if (S.kind == SEG_SWIGLU_BF16) {
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + n0;
+          for (int l = 0; l < 16; ++l) part[l] = __fadd_rn(part[l], pbuf[l]);
 #pragma unroll
-            for (int i = 0; i < 128; i += 8) {
-              uint4 w4 = make_uint4(pack_bf16x2(acc[i], acc[i + 1]), pack_bf16x2(acc[i + 2], acc[i + 3]),
-                                    pack_bf16x2(acc[i + 4], acc[i + 5]), pack_bf16x2(acc[i + 6], acc[i + 7]));
-              *reinterpret_cast<uint4*>(o + i) = w4;
-            }
-          } else {
-          hadamard128_regs(acc);
-          float amax = 0.0f;
+          for (int off = 8; off; off >>= 1)
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            acc[i] = __fmul_rn(acc[i], kHadamardScale);
-            amax = fmaxf(amax, fabsf(acc[i]));
-          }
-          const __half hs = group_scale(amax);
-          const float sd = __half2float(hs);
-          const int grp = n0 / 128;  // output group (128 columns) index
-          S.out_scale[(int64_t)row * (S.n / 128) + grp] = hs;
-          uint8_t* o = reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld + grp * 64;
-          const float rcp = sd > 0.0f ? __frcp_rn(sd) : 0.0f;
+            for (int l = 0; l < off; ++l) part[l] = __fadd_rn(part[l], part[l + off]);
+          pbuf[16] = __frsqrt_rn(__fadd_rn(__fmul_rn(part[0], 0.0078125f), S.eps));
+        }
+        epi_barrier();
+        const float inv = pbuf[16];
+        if (row_ok) {
+          const int token = row % p.length;
+          const int hc0 = (cq & 1) * 64;  // column of this thread's first value within the head
+          const float* f = p.freqs + (int64_t)token * 256 + 2 * hc0;
+          const float* nw = S.normw + hc0;
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + col0;
 #pragma unroll
-          for (int i = 0; i < 128; i += 32) {
+          for (int i = 0; i < 64; i += 8) {
             uint32_t w[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint32_t word = 0;
-              if (sd > 0.0f) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                  word |= (uint32_t)(quant_code(acc[i + 8 * j + e], sd, rcp) & 0xF) << (4 * e);
-              }
-              w[j] = word;
+            for (int j = 0; j < 8; j += 2) {
+              const int c = i + j;
+              const float a = bf16_round(__fmul_rn(__fmul_rn(acc[c], inv), __fadd_rn(nw[c], 1.0f)));
+              const float bb = bf16_round(__fmul_rn(__fmul_rn(acc[c + 1], inv), __fadd_rn(nw[c + 1], 1.0f)));
+              const float4 fr = __ldg(reinterpret_cast<const float4*>(f + 2 * c));
+              const float o0 = __fmaf_rn(fr.x, a, __fmul_rn(fr.y, bb));
+              const float o1 = __fmaf_rn(fr.z, a, __fmul_rn(fr.w, bb));
+              w[j / 2] = pack_bf16x2(o0, o1);
             }
-            *reinterpret_cast<uint4*>(o + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(o + i) = make_uint4(w[0], w[1], w[2], w[3]);
           }
+        }
+      } else if (pairw) {
+        // Quarters 0/1 hold gate columns 0-63 / 64-127 of the 128 output
+        // columns, quarters 2/3 the up columns; the up quarters hand bf16(up)
+        // to their gate partner through shared memory.
+        const int h = cq & 1;  // which 64-column half of the output group
+        float* ubuf = xch + (h * 128 + rloc) * 65;
+        if (cq >= 2) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) ubuf[i] = bf16_round(acc[i]);
+        }
+        epi_barrier();
+        if (cq < 2) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float gv = bf16_round(acc[i]);
+            const float av = bf16_round(silu_contract(gv));
+            acc[i] = bf16_round(__fmul_rn(av, ubuf[i]));
+          }
+        }
+        if (S.kind == SEG_SWIGLU_BF16) {
+          if (cq < 2 && row_ok)
+            store_bf16x64(reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + n0 + h * 64, acc);
+        } else {
+          // H128 over the pair: stages 1..32 inside each half, stage 64 across.
+          float* hbuf = xch + 2 * 128 * 65 + (h * 128 + rloc) * 66;
+          const float* other = xch + 2 * 128 * 65 + ((h ^ 1) * 128 + rloc) * 66;
+          if (cq < 2) {
+            hadamard64_regs(acc);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) hbuf[i] = acc[i];
+          }
+          epi_barrier();
+          float amax = 0.0f;
+          if (cq < 2) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              // element i of the lower half pairs with element i of the upper half
+              const float a = h ? other[i] : acc[i];
+              const float b = h ? acc[i] : other[i];
+              acc[i] = __fmul_rn(h ? __fsub_rn(a, b) : __fadd_rn(a, b), kHadamardScale);
+              amax = fmaxf(amax, fabsf(acc[i]));
+            }
+          }
+          epi_barrier();  // both halves have read each other's stage-32 values
+          if (cq < 2) hbuf[64] = amax;
+          epi_barrier();
+          if (cq < 2) {
+            amax = fmaxf(amax, other[64]);
+            const __half hs = group_scale(amax);
+            const float sd = __half2float(hs);
+            const int grp = n0 / 128;  // output group (128 columns) index
+            if (row_ok) {
+              if (h == 0) S.out_scale[(int64_t)row * (S.n / 128) + grp] = hs;
+              uint8_t* o = reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld + grp * 64 + h * 32;
+              const float rcp = sd > 0.0f ? __frcp_rn(sd) : 0.0f;
+#pragma unroll
+              for (int i = 0; i < 64; i += 32) {
+                uint32_t w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  uint32_t word = 0;
+                  if (sd > 0.0f) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                      word |= (uint32_t)(quant_code(acc[i + 8 * j + e], sd, rcp) & 0xF) << (4 * e);
+                  }
+                  w[j] = word;
+                }
+                *reinterpret_cast<uint4*>(o + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            }
           }
         }
       }

@@ -205,6 +205,42 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// 32 lanes x 32 columns of 32-bit.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld_regs32(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
+                 "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+// Writes the same 32-bit value into 8 consecutive columns of each of the
+// warp's 32 lanes (a wider form would need that many registers holding it).
+__device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+// 64 columns starting at taddr.
+__device__ __forceinline__ void tmem_fill64(uint32_t taddr, uint32_t v) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tmem_fill8(taddr + 8 * i, v);
+}
+__device__ __forceinline__ void setmaxnreg_dec32() { asm volatile("setmaxnreg.dec.sync.aligned.u32 32;"); }
+__device__ __forceinline__ void setmaxnreg_inc112() { asm volatile("setmaxnreg.inc.sync.aligned.u32 112;"); }
+
 // UMMA shared-memory descriptor for a 128B-swizzled tile (sm_100 version 1).
 // K-major: rows of 128 B, 8-row atoms 1024 B apart (SBO), LBO unused (1).
 // MN-major: 128 B of MN per K row, 8 K rows per atom (SBO between K atoms),
@@ -228,6 +264,24 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt
 }
 
 // ------------------------------------------------------- packed fp32 math
+// Float pairs kept in 64-bit registers so fma.rn.f32x2 consumes them without
+// repacking.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+// acc = fma(fma({x0,x1}, sa, sb), sw, acc) on a float pair, the two drained
+// TMEM words x0/x1 given as raw bits.
+__device__ __forceinline__ void dequant_acc2(uint64_t& acc, uint32_t x0, uint32_t x1, uint64_t sa2, uint64_t sb2,
+                                             uint64_t sw2) {
+  asm("{\n\t.reg .b64 f, u;\n\tmov.b64 f, {%1, %2};\n\tfma.rn.f32x2 u, f, %3, %4;\n\tfma.rn.f32x2 %0, u, %5, "
+      "%0;\n\t}"
+      : "+l"(acc)
+      : "r"(x0), "r"(x1), "l"(sa2), "l"(sb2), "l"(sw2));
+}
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   float2 d;
   asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, "

@@ -206,6 +206,12 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
   if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_w4a4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
+    // setmaxnreg splits exactly the registers the CTA is launched with: any
+    // other allocation could leave a warpgroup waiting for registers.
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, gemm_w4a4_kernel);
+    if (e != cudaSuccess) return (int)e;
+    if (fa.numRegs != GEMM_LAUNCH_REGS) return (int)cudaErrorInvalidConfiguration;
     attr_set[dev] = true;
   }
   dim3 grid((M + GEMM_BM - 1) / GEMM_BM, tiles);
