@@ -150,3 +150,58 @@ K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, vo
   }
   return 0;
 }
+
+// ----------------------------------------------------------------------------
+// Block loop without any allocation by the caller.
+//
+// Some callers cannot call cudaMalloc: an embedding host that owns the device
+// allocator (its own pool or arena) and forbids other libraries from
+// allocating, or a plugin that is handed only the input/output buffers.  This
+// entry point takes the same inputs and outputs as k2b_forward_blocks but
+// carves its workspace out of a fixed file-scope device array instead of a
+// caller-provided buffer.
+//
+// Limit: kStaticWorkspaceBytes (64 MiB).  With the Krea2 widths (hidden 6144,
+// 48/12 heads, MLP 16384) the workspace takes ~45.5 KB per token row, so up to
+// ~1470 rows (batch * length) per call; larger requests are rejected with
+// cudaErrorInvalidValue (k2b_static_workspace_bytes() reports the limit).
+// The array is a static device variable: every device that loads the library
+// keeps it for the life of the process.
+//
+// Set-up: the first call on a device (with that device current) resolves the
+// array's device address with cudaGetSymbolAddress; make that first call
+// outside any CUDA stream capture.  Every call shares the one array, and the
+// kernels overwrite every workspace byte they read (nothing needs to start at
+// zero), so calls whose executions overlap on the GPU (different streams, or
+// different host threads on the same device) race on it and must be
+// serialised by the caller.
+// ----------------------------------------------------------------------------
+namespace k2b {
+constexpr size_t kStaticWorkspaceBytes = size_t(64) << 20;
+static __device__ __align__(256) uint8_t g_static_workspace[kStaticWorkspaceBytes];
+}  // namespace k2b
+
+K2B_EXPORT long long k2b_static_workspace_bytes(void) { return (long long)k2b::kStaticWorkspaceBytes; }
+
+K2B_EXPORT int k2b_forward_blocks_static(const void* const* block_ptrs, int nblocks, void* x, const void* freqs,
+                                         int batch, int length, int hidden, int heads, int kvheads, int mlp, float eps,
+                                         float qk_eps, void* stream) {
+  using namespace k2b;
+  if (batch <= 0 || length <= 0 || hidden <= 0 || heads <= 0 || kvheads <= 0 || mlp <= 0)
+    return (int)cudaErrorInvalidValue;
+  const long long need = k2b_block_workspace_bytes((int)((long long)batch * length), hidden, heads, kvheads, mlp);
+  if (need <= 0 || need > (long long)kStaticWorkspaceBytes) return (int)cudaErrorInvalidValue;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_workspace);
+    if (e != cudaSuccess) return (int)e;
+    addr[dev] = p;
+  }
+  return k2b_forward_blocks(block_ptrs, nblocks, x, freqs, addr[dev], (long long)kStaticWorkspaceBytes, batch, length,
+                            hidden, heads, kvheads, mlp, eps, qk_eps, nullptr, stream);
+}

@@ -34,6 +34,8 @@ SIGNATURES = {
     "k2b_block_slots": (_I, []),
     "k2b_block_workspace_bytes": (_LL, [_I] * 5),
     "k2b_forward_blocks": (_I, [_P, _I, _P, _P, _P, _LL, _I, _I, _I, _I, _I, _I, _F, _F, _P, _P]),
+    "k2b_static_workspace_bytes": (_LL, []),
+    "k2b_forward_blocks_static": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _F, _F, _P]),
     "k2_norm_mod_quant4": (_I, [_P] * 6 + [_I] * 5 + [_F, _I, _I, _P]),
     "k2_int4_qkv": (_I, [_P] * 17 + [_I] * 5 + [_F, _F, _P]),
     "k2_int4_swiglu": (_I, [_P] * 7 + [_I] * 4 + [_P]),

@@ -150,6 +150,20 @@ int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, cons
                        long long workspace_bytes, int batch, int length, int hidden, int heads, int kvheads, int mlp,
                        float eps, float qk_eps, void* const* events, void* stream);
 
+/* Block loop that allocates nothing, for callers that cannot call cudaMalloc
+ * (an embedding host that owns the device allocator, a plugin handed only its
+ * input/output buffers).  No counterpart in the reference: it is
+ * k2b_forward_blocks with the workspace taken from a file-scope device array
+ * of k2b_static_workspace_bytes() (64 MiB; ~1470 token rows at the Krea2
+ * widths); larger batch*length is rejected with cudaErrorInvalidValue.  The
+ * first call on each device resolves the array's address (cudaGetSymbolAddress)
+ * and must come before any stream capture; calls that overlap on the GPU race
+ * on the shared array.  Nothing in it needs to start at zero. */
+long long k2b_static_workspace_bytes(void);
+int k2b_forward_blocks_static(const void* const* block_ptrs, int nblocks, void* x, const void* freqs, int batch,
+                              int length, int hidden, int heads, int kvheads, int mlp, float eps, float qk_eps,
+                              void* stream);
+
 /* -------------------------------------- reference-named exports (shims) --
  * Same names and argument order as the reference's kernel libraries so that
  * native_runtime.cpp's configure()/configure_joint()/configure_norm_quant()
