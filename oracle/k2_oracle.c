@@ -34,11 +34,19 @@ static inline uint32_t f_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u
 
 float k2o_bf16_to_f32(uint16_t h) { return bits_f((uint32_t)h << 16); }
 
-/* round-to-nearest-even fp32 -> bf16 (NaN kept quiet), like __float2bfloat16_rn */
+/* fp32 -> bf16 rounding mode.  0 (default): round to nearest even, like
+ * __float2bfloat16_rn on the GPU -- the contract.  1: truncation, which is what
+ * the Triton CPU interpreter does for .to(tl.bfloat16); used only to compare
+ * bit for bit with the reference's Triton kernels run under that interpreter
+ * (tests/golden). */
+static int g_bf16_truncate = 0;
+void k2o_set_bf16_truncate(int on) { g_bf16_truncate = on; }
+
+/* fp32 -> bf16 (NaN kept quiet) */
 uint16_t k2o_f32_to_bf16(float f) {
     uint32_t u = f_bits(f);
     if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
-    u += 0x7fffu + ((u >> 16) & 1u);
+    if (!g_bf16_truncate) u += 0x7fffu + ((u >> 16) & 1u);
     return (uint16_t)(u >> 16);
 }
 static inline float bf(uint16_t h) { return k2o_bf16_to_f32(h); }

@@ -72,6 +72,7 @@ def _declare(L):
     L.k2o_sigmoid_gate.argtypes = [P, I64, P]
     L.k2o_exp_vec.argtypes = [P, P, I64]
     L.k2o_bf16_round_vec.argtypes = [P, P, I64]
+    L.k2o_set_bf16_truncate.argtypes = [I]
     L.k2o_exp.argtypes = [F]
     L.k2o_exp.restype = F
     L.k2o_rsqrt_rn.argtypes = [F]
@@ -97,6 +98,18 @@ def _row_blocks(n: int, parts: int):
 
 
 # ----------------------------------------------------------------- bf16 helpers
+
+class bf16_truncation:
+    """Context manager: bf16 conversions truncate instead of rounding to
+    nearest even (only to compare with kernels run under the Triton CPU
+    interpreter, which truncates)."""
+
+    def __enter__(self):
+        lib().k2o_set_bf16_truncate(1)
+
+    def __exit__(self, *exc):
+        lib().k2o_set_bf16_truncate(0)
+
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 bit patterns, round to nearest even."""

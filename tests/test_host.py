@@ -1,0 +1,58 @@
+"""Host-side logic of the k2b package (no GPU): RoPE positions and table,
+argument validation of the torch wrappers, the work accounting bench.py uses."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+
+def test_rope_table_matches_oracle_restatement():
+    from k2b.model import rope_positions, rope_table
+
+    pos = rope_positions(98, 76, 52)
+    assert pos.shape == (4050, 2)
+    t = rope_table(pos, (64, 64), 10000.0)
+    assert t.shape == (4050, 64, 2, 2) and t.dtype == torch.float32
+    ref = O.rope_table(pos.numpy(), (64, 64), 10000.0)
+    assert np.array_equal(t.numpy(), ref)
+
+
+def test_rope_positions_layout():
+    from k2b.model import rope_positions
+
+    pos = rope_positions(128, 64, 64).numpy()
+    assert pos.shape == (4224, 2)
+    assert np.array_equal(pos[:128, 0], np.arange(128)) and np.array_equal(pos[:128, 0], pos[:128, 1])
+    assert pos[128].tolist() == [128.0, 128.0] and pos[128 + 65].tolist() == [129.0, 129.0]
+
+
+def test_ops_reject_cpu_tensors():
+    from k2b import ops
+
+    x = torch.zeros(4, 512, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.rotate_quant(x)
+    with pytest.raises(ValueError):
+        ops.attention(torch.zeros(1, 2, 4, 128, dtype=torch.bfloat16), torch.zeros(1, 1, 4, 128, dtype=torch.bfloat16),
+                      torch.zeros(1, 1, 4, 128, dtype=torch.bfloat16), mask=torch.ones(4, 4, dtype=torch.bool))
+
+
+def test_block_work_accounting_matches_baseline_figures():
+    from k2b.model import ModelConfig, block_flops
+
+    cfg = ModelConfig()
+    f = block_flops(cfg, 4050, 4050, 1)
+    assert round(f["qkv"] / 1e9, 2) == 458.65
+    assert round(f["attn"] / 1e9, 2) == 403.11
+    assert round(f["int_ops"] / 1e9, 1) == 3210.5
+
+
+def test_norm_weight_w_plus_one_form_is_exact():
+    from k2b.model import _norm_weight
+
+    g = torch.Generator().manual_seed(0)
+    w = _norm_weight(6144, g, "cpu")
+    w_eff = w + 1.0
+    assert torch.equal(w_eff, w_eff.to(torch.bfloat16).to(torch.float32))
+    assert float(w_eff.min()) >= 0.89 and float(w_eff.max()) <= 1.11
