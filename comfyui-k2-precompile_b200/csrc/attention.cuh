@@ -317,26 +317,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           hadamard128_regs(o);
           float amax = 0.0f;
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            o[i] = __fmul_rn(o[i], kHadamardScale);
-            amax = fmaxf(amax, fabsf(o[i]));
-          }
-          const __half hs = group_scale(amax);
-          const float sd = __half2float(hs);
-          p.os[orow * p.heads + h] = hs;
-          const float rcp = sd > 0.0f ? __frcp_rn(sd) : 0.0f;
+          for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(o[i]));
+          const QuantGroup qg = quant_group(amax);
+          p.os[orow * p.heads + h] = qg.scale;
           uint8_t* dq = p.oq + orow * (p.heads * FA_D / 2) + h * 64;
 #pragma unroll
           for (int i = 0; i < 128; i += 32) {
             uint32_t w[4];
 #pragma unroll
             for (int jw = 0; jw < 4; ++jw) {
-              uint32_t word = 0;
-              if (sd > 0.0f) {
+              uint32_t b[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) word |= (uint32_t)(quant_code(o[i + 8 * jw + e], sd, rcp) & 0xF) << (4 * e);
-              }
-              w[jw] = word;
+              for (int e = 0; e < 8; ++e) b[e] = quant_bits(o[i + 8 * jw + e], qg.c, qg.clamp);
+              w[jw] = pack8_codes(b);
             }
             *reinterpret_cast<uint4*>(dq + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
           }

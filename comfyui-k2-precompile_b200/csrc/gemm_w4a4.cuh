@@ -106,10 +106,12 @@ __device__ __forceinline__ void unpack_chunk(uint4 v, uint4& lo, uint4& hi) {
   lo.w = (v.w << 4) & 0xF0F0F0F0u; hi.w = v.w & 0xF0F0F0F0u;
 }
 
-// Sylvester H128 stages h = 1..32 on 64 consecutive values held by one thread.
+// Hadamard stages h = 2, 4, 8, 1, 16, 32 (the contract's order without the
+// final h = 64) on 64 consecutive values held by one thread.
 __device__ __forceinline__ void hadamard64_regs(float (&v)[64]) {
 #pragma unroll
-  for (int lh = 0; lh < 6; ++lh) {
+  for (int st = 0; st < 6; ++st) {
+    const int lh = hadamard_stage_bit(st);
     const int h = 1 << lh;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -492,7 +494,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               // element i of the lower half pairs with element i of the upper half
               const float a = h ? other[i] : acc[i];
               const float b = h ? acc[i] : other[i];
-              acc[i] = __fmul_rn(h ? __fsub_rn(a, b) : __fadd_rn(a, b), kHadamardScale);
+              acc[i] = h ? __fsub_rn(a, b) : __fadd_rn(a, b);
               amax = fmaxf(amax, fabsf(acc[i]));
             }
           }
@@ -501,25 +503,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           epi_barrier();
           if (cq < 2) {
             amax = fmaxf(amax, other[64]);
-            const __half hs = group_scale(amax);
-            const float sd = __half2float(hs);
+            const QuantGroup qg = quant_group(amax);
             const int grp = n0 / 128;  // output group (128 columns) index
             if (row_ok) {
-              if (h == 0) S.out_scale[(int64_t)row * (S.n / 128) + grp] = hs;
+              if (h == 0) S.out_scale[(int64_t)row * (S.n / 128) + grp] = qg.scale;
               uint8_t* o = reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld + grp * 64 + h * 32;
-              const float rcp = sd > 0.0f ? __frcp_rn(sd) : 0.0f;
 #pragma unroll
               for (int i = 0; i < 64; i += 32) {
                 uint32_t w[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                  uint32_t word = 0;
-                  if (sd > 0.0f) {
+                  uint32_t b[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                      word |= (uint32_t)(quant_code(acc[i + 8 * j + e], sd, rcp) & 0xF) << (4 * e);
-                  }
-                  w[j] = word;
+                  for (int e = 0; e < 8; ++e) b[e] = quant_bits(acc[i + 8 * j + e], qg.c, qg.clamp);
+                  w[j] = pack8_codes(b);
                 }
                 *reinterpret_cast<uint4*>(o + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
               }

@@ -298,12 +298,19 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 // ------------------------------------------------- exact scalar contract
 
-// In-register Sylvester H128 on 128 fp32 values: stages h = 1, 2, ..., 64 in
-// that order, (a, b) -> (a + b, a - b) (oracle: k2o_hadamard128 before its
-// final scaling).  Counted stage loop so every index is a compile-time constant.
+// Unnormalised Walsh-Hadamard transform of a 128-column group: seven
+// butterfly stages (a, b) -> (a + b, a - b) over index bit lh (partner
+// distance h = 1 << lh), each sum rounded to fp32, in the contract's order
+// h = 2, 4, 8, 1, 16, 32, 64 (oracle: k2o_hadamard128).  Any stage order
+// gives the same transform in exact arithmetic; this one lets the
+// norm_quant kernel run every stage but one on packed f32x2 pairs.
+__host__ __device__ constexpr int hadamard_stage_bit(int st) { return st < 3 ? st + 1 : (st == 3 ? 0 : st); }
+// In-register transform of 128 fp32 values; counted stage loop so every
+// index is a compile-time constant.
 __device__ __forceinline__ void hadamard128_regs(float (&v)[128]) {
 #pragma unroll
-  for (int lh = 0; lh < 7; ++lh) {
+  for (int st = 0; st < 7; ++st) {
+    const int lh = hadamard_stage_bit(st);
     const int h = 1 << lh;
 #pragma unroll
     for (int i = 0; i < 64; ++i) {
@@ -355,22 +362,81 @@ __device__ __forceinline__ float sigmoid_contract(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_contract(-x)));
 }
 
-// INT4 code of v for the dequant scale sd > 0: clamp(rint(v / sd), -8, 7)
-// with a correctly rounded division.  The product with the reciprocal picks
-// the same integer unless v/sd lies within ~1e-6 of a half-integer, where the
-// exact division decides.
-__device__ __forceinline__ int quant_code(float v, float sd, float rcp) {
-  float t = __fmul_rn(v, rcp);
-  float r = rintf(t);
-  if (fabsf(fabsf(__fsub_rn(t, r)) - 0.5f) < 1.0e-3f) r = rintf(__fdiv_rn(v, sd));
-  r = fminf(fmaxf(r, -8.0f), 7.0f);
-  return (int)r;
+// ------------------------------------------- group-128 INT4 quantisation
+// Input: the 128 raw outputs u of hadamard128_regs (no 1/sqrt(128) applied).
+// Contract (oracle: k2o_quant_group128):
+//   scale = fp16(min(fp32(max|u| * kQuantScale), 65504)),
+//           kQuantScale = fp32(1 / (7 * sqrt(128)))
+//   c     = fp32(kHadamardScale * fp32(1 / scale))     (0 for a zero scale)
+//   code  = clamp(rne(u * c), -8, 7)                    (exact product)
+// The rounding is one fma(u, c, 1.5*2^23 + 8): the sum lies on the integer
+// grid, so its fp32 bits are 0x4B400000 + (code + 8) and the low nibble holds
+// the offset-8 code.  When the scale is a normal fp16 that was not clamped,
+// |u * c| <= 7 * (1 + 2^-11 + 2^-21) < 7.5, so the clamp cannot bind and is
+// skipped.  Codes of NaN inputs are unspecified (the scale ignores NaN).
+constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
+constexpr float kRoundMagic8 = 12582920.0f;  // 1.5 * 2^23 + 8
+constexpr float kQuantScale = 0.012626906856894493103027343750f;
+struct QuantGroup {
+  __half scale;
+  float sd;  // the scale as fp32
+  float c;
+  bool clamp;
+};
+__device__ __forceinline__ QuantGroup quant_scale(float amax_raw) {
+  QuantGroup g;
+  const float sf = __fmul_rn(amax_raw, kQuantScale);
+  g.scale = __float2half_rn(fminf(sf, 65504.0f));
+  g.sd = __half2float(g.scale);
+  g.c = 0.0f;
+  g.clamp = !(g.sd >= 6.103515625e-05f) || !(sf <= 65504.0f);
+  return g;
 }
-// fp16 scale of a group with absolute maximum amax: fp16(min(amax/7, 65504)).
-__device__ __forceinline__ __half group_scale(float amax) {
-  float sf = __fdiv_rn(amax, 7.0f);
-  sf = fminf(sf, 65504.0f);
-  return __float2half_rn(sf);
+__device__ __forceinline__ QuantGroup quant_group(float amax_raw) {
+  QuantGroup g = quant_scale(amax_raw);
+  g.c = g.sd > 0.0f ? __fmul_rn(kHadamardScale, __frcp_rn(g.sd)) : 0.0f;
+  return g;
+}
+// Table form of c: with sd = m * 2^e (m in [1, 2)), fp32(1/sd) = 2^-e *
+// fp32(1/m) and fp32(H * 2^-e * r) = 2^-e * fp32(H * r), because scaling by a
+// power of two is exact while everything stays normal (every positive fp16,
+// its reciprocal and H times it do).  So tab[i] = fp32(H * fp32(1 / (1 +
+// i/1024))) over the 1024 fp16 significands gives the contract's c exactly;
+// fp16 subnormals are normal fp32 and index the same table.
+__device__ __forceinline__ void quant_table_init(float* tab, int tid, int nthreads) {
+  for (int i = tid; i < 1024; i += nthreads)
+    tab[i] = __fmul_rn(kHadamardScale, __frcp_rn(1.0f + (float)i * (1.0f / 1024.0f)));
+}
+__device__ __forceinline__ float quant_c_table(float sd, const float* tab) {
+  const uint32_t b = __float_as_uint(sd);
+  const uint32_t t = __float_as_uint(tab[(b >> 13) & 1023u]);
+  return b ? __uint_as_float(t - ((b & 0x7F800000u) - 0x3F800000u)) : 0.0f;
+}
+// fp32 bits 0x4B400000 + (code + 8): low nibble = code + 8, bits 4..21 zero.
+__device__ __forceinline__ uint32_t quant_bits(float u, float c, bool clamp) {
+  float r = __fmaf_rn(u, c, kRoundMagic8);
+  if (clamp) r = fminf(fmaxf(r, kRoundMagic), kRoundMagic + 15.0f);
+  return __float_as_uint(r);
+}
+// Sum of 0x4B400000 << 4j over j = 0..7, mod 2^32: what the exponent bits of
+// eight quant_bits words add to an 8-nibble shift-and-add pack.
+__host__ __device__ constexpr uint32_t pack_bias8() {
+  uint32_t s = 0;
+  for (int j = 0; j < 8; ++j) s += 0x4B400000u << (4 * j);
+  return s;
+}
+// Eight quant_bits words -> eight two's-complement nibbles, element j in
+// bits 4j..4j+3.  Bits 4..21 of every word are zero, so the shifted sum of
+// the low nibbles carries nothing; the exponent bits add a known constant.
+__device__ __forceinline__ uint32_t pack8_codes(const uint32_t (&b)[8]) {
+  uint32_t s = b[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) s += b[j] << (4 * j);
+  return (s - pack_bias8()) ^ 0x88888888u;
+}
+// Two quant_bits words -> one byte of two's-complement nibbles (even low).
+__device__ __forceinline__ uint32_t pack2_codes(uint32_t b0, uint32_t b1) {
+  return (((b1 << 4) + b0) ^ 0x88u) & 0xFFu;
 }
 
 }  // namespace k2b

@@ -76,32 +76,33 @@ static int launch_status() { return (int)cudaGetLastError(); }
 template <bool NORM>
 static int norm_quant_launch(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                              int rows, int K, int length, int cut, int batch, float eps, cudaStream_t st) {
-  if (rows <= 0 || K <= 0 || K % 512 || (NORM && (length <= 0 || batch <= 0))) return (int)cudaErrorInvalidValue;
-  if (!aligned16(x) || !aligned16(q) || (NORM && (!aligned16(w) || !aligned16(scale) || !aligned16(shift))))
+  if (rows <= 0 || K <= 0 || K % 512 || K > 16384 || (NORM && (length <= 0 || batch <= 0)))
     return (int)cudaErrorInvalidValue;
-  const auto* xb = static_cast<const __nv_bfloat16*>(x);
-  const auto* wf = static_cast<const float*>(w);
-  const auto* sc = static_cast<const __nv_bfloat16*>(scale);
-  const auto* sh = static_cast<const __nv_bfloat16*>(shift);
-  auto* qo = static_cast<uint8_t*>(q);
-  auto* so = static_cast<__half*>(s);
-  switch (K / 512) {
-#define K2B_NQ_CASE(S)                                                                                \
-  case S:                                                                                             \
-    norm_quant_kernel<S, NORM><<<rows, 128, 0, st>>>(xb, wf, sc, sh, qo, so, length, cut, batch, eps); \
-    break;
-    K2B_NQ_CASE(1)
-    K2B_NQ_CASE(2)
-    K2B_NQ_CASE(4)
-    K2B_NQ_CASE(8)
-    K2B_NQ_CASE(12)
-    K2B_NQ_CASE(16)
-    K2B_NQ_CASE(24)
-    K2B_NQ_CASE(32)
-#undef K2B_NQ_CASE
-    default:
-      return (int)cudaErrorInvalidValue;
+  if (!aligned16(x) || !aligned16(q) || !s || (NORM && (!aligned16(w) || !aligned16(scale) || !aligned16(shift))))
+    return (int)cudaErrorInvalidValue;
+  // One wave of resident CTAs looping over 16-row tiles; the residency is
+  // queried once per device (the same value may be stored twice by racing
+  // first calls, which is harmless).
+  static int resident[2][64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+  int& per_sm = resident[NORM ? 1 : 0][dev];
+  if (per_sm == 0) {
+    int n = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, norm_quant_kernel<NORM>, kNqThreads, 0);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return (int)e;
+    per_sm = (n > 0 ? n : 1) * sms;
   }
+  const int tiles = (rows + kNqRows - 1) / kNqRows;
+  const int grid = tiles < per_sm ? tiles : per_sm;
+  norm_quant_kernel<NORM><<<grid, kNqThreads, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(w), static_cast<const __nv_bfloat16*>(scale),
+      static_cast<const __nv_bfloat16*>(shift), static_cast<uint8_t*>(q), static_cast<__half*>(s), rows, K, length,
+      cut, batch, eps);
   return launch_status();
 }
 

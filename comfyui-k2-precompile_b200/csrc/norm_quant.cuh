@@ -2,129 +2,282 @@
 // group-128 INT4 pack, and its rotation-only twin (rotate_quant).
 //
 // Replaces kernels/norm_quant.cu:11-67 (norm_mod_quant) of the reference.
-// Layout: one CTA of 128 threads per row.  Thread t loads columns
-// 512*i + 4t .. +3 for every 512-column slab i (8-byte loads, 1 KB per warp
-// instruction), which is exactly the lane partition of the reference's
-// sum-of-squares (kernels/norm_quant.cu:20-31), so the fp32 reduction order
-// is reproduced without any reshuffle.  In slab i, warp w holds the 128-column
-// quantisation group 4i + w (4 consecutive columns per lane): the Hadamard
-// stages h = 1, 2 run in registers and h = 4..64 as lane-xor shuffles.
+//
+// HBM traffic per row of K bf16: 2K bytes read, K/2 code bytes + K/64 scale
+// bytes written.  Organisation:
+//
+// * A CTA (4 warps) owns a tile of kNqRows rows and loops over tiles
+//   (persistent grid, one wave of resident CTAs).
+// * Stage A (NORM only), one warp per row: lane l loads columns 512i + 16l
+//   .. +15 of every 512-column slab i.  Those are the columns of the
+//   reference's sum-of-squares lanes 4l..4l+3 (kernels/norm_quant.cu:20-26:
+//   lane r owns 512i + 4r .. +3), so each lane runs those four fmaf chains in
+//   the reference's order, and the reference's shfl_down tree (offsets 16, 8,
+//   4, 2, 1, then (w2 + w0) + (w3 + w1)) is replayed as width-8 shuffles
+//   plus in-lane adds: the fp32 sum is the reference's bit for bit.
+// * Stage B, column-stationary: warp w takes slabs w, w+4, ...; lane l keeps
+//   the modulation constants of its 16 columns in registers for every row of
+//   the tile, re-reads x (an L2 hit; two row buffers alternate), modulates,
+//   and runs the Hadamard:
+//     layout A (lane owns 16 consecutive columns, pairs (e, e+1)): stages
+//       h = 2, 4, 8 on packed f32x2;
+//     a shared-memory transpose to layout B (lane v of a group owns
+//       e = 2v + b0 + 16m, m = 0..7, pairs (e, e+1)): stage h = 1 (inside
+//       each pair) and h = 16, 32, 64 on packed f32x2.
+//   The 8 lanes of a group then reduce max|u| with 3 xor-shuffles, quantise
+//   (one fma per element), and stage the 64 code bytes in shared memory so
+//   every warp writes its 256 code bytes with one 8-byte store per lane.
 #pragma once
 #include "k2b_common.cuh"
 
 namespace k2b {
 
-template <int SLABS, bool NORM>
-__global__ void __launch_bounds__(128) norm_quant_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         const float* __restrict__ w,
-                                                         const __nv_bfloat16* __restrict__ scale,
-                                                         const __nv_bfloat16* __restrict__ shift,
-                                                         uint8_t* __restrict__ q, __half* __restrict__ s,
-                                                         int length, int cut, int batch, float eps) {
-  constexpr int K = SLABS * 512;
-  constexpr int G = K / 128;
-  const int row = blockIdx.x;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const __nv_bfloat16* xr = x + (int64_t)row * K;
+constexpr int kNqThreads = 128;  // 4 warps
+constexpr int kNqRows = 8;       // rows per tile
 
-  uint2 raw[SLABS];
-#pragma unroll
-  for (int i = 0; i < SLABS; ++i) raw[i] = __ldg(reinterpret_cast<const uint2*>(xr + 512 * i + 4 * t));
+__device__ __forceinline__ float2 bf2_unpack(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __nv_bfloat162 bf2_from(uint32_t w) { return *reinterpret_cast<__nv_bfloat162*>(&w); }
+// (a + b, a - b) for packed pairs; fma(b, -1, a) is a - b rounded once.
+__device__ __forceinline__ void bfly2(float2& a, float2& b) {
+  const float2 s = __fadd2_rn(a, b);
+  b = __ffma2_rn(b, make_float2(-1.0f, -1.0f), a);
+  a = s;
+}
+// max(a, b, c) in one instruction (NaN operands are ignored, as by fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// Per-warp transpose buffer: group g (128 fp32) at 144*g floats, logical
+// 16-byte chunk c at chunk c + c/8.  The layout-A stores (lane u of a group
+// writes chunks 4u..4u+3, 8 lanes per wavefront) land on chunks
+// 4u + u/2 + k: eight distinct bank quads; the layout-B 8-byte loads (lane v
+// reads pair v of chunk row m, 16 lanes per wavefront) cover 16 consecutive
+// banks per group and groups g, g+1 sit 16 banks apart.  Every address is a
+// per-lane base plus a compile-time offset.
+constexpr int kNqGroupFloats = 144;
+__device__ __forceinline__ constexpr int nq_pad_chunk(int c) { return c + (c >> 3); }
 
-  float inv = 1.0f;
-  int b = 0;
-  if constexpr (NORM) {
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < SLABS; ++i) {
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float2 f = __bfloat1622float2(h2[j]);
-        sum = __fmaf_rn(f.x, f.x, sum);
-        sum = __fmaf_rn(f.y, f.y, sum);
-      }
-    }
-#pragma unroll
-    for (int off = 16; off; off >>= 1) sum = __fadd_rn(sum, __shfl_down_sync(0xffffffffu, sum, off));
-    __shared__ float warp_sums[4];
-    if (lane == 0) warp_sums[warp] = sum;
-    __syncthreads();
-    const float total = __fadd_rn(__fadd_rn(warp_sums[2], warp_sums[0]), __fadd_rn(warp_sums[3], warp_sums[1]));
-    inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), eps));
-    b = row / length;
-    if (cut >= 0 && row % length >= cut) b += batch;
-  }
+template <bool NORM>
+__global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                const float* __restrict__ w,
+                                                                const __nv_bfloat16* __restrict__ scale,
+                                                                const __nv_bfloat16* __restrict__ shift,
+                                                                uint8_t* __restrict__ q, __half* __restrict__ s,
+                                                                int rows, int K, int length, int cut, int batch,
+                                                                float eps) {
+  __shared__ float s_inv[kNqRows];
+  __shared__ int s_lat[kNqRows];  // modulation row (latent) of each tile row
+  __shared__ __align__(16) float s_tr[4][4 * kNqGroupFloats];
+  __shared__ __align__(16) uint8_t s_codes[4][320];
+  __shared__ float s_rcp[1024];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 3, v = lane & 7;  // group within the slab, lane within the group
+  const int slabs = K >> 9;
+  const int tiles = (rows + kNqRows - 1) / kNqRows;
+  float* tr = s_tr[warp] + g * kNqGroupFloats;
+  float* tra = tr + 4 * nq_pad_chunk(4 * v);                   // layout-A store base
+  const float* trb = tr + 4 * (v >> 1) + 2 * (v & 1);          // layout-B load base
+  uint8_t* cb = s_codes[warp];
+  const int cpos = 64 * g + 16 * (g >> 1);  // this group's 64 code bytes in cb
+  quant_table_init(s_rcp, threadIdx.x, kNqThreads);
+  __syncthreads();
 
-  uint8_t* qr = q + (int64_t)row * (K / 2);
-  __half* sr = s + (int64_t)row * G;
-#pragma unroll
-  for (int i = 0; i < SLABS; ++i) {
-    const int col = 512 * i + 4 * t;
-    float v[4];
-    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
-    {
-      float2 a = __bfloat1622float2(h2[0]), c = __bfloat1622float2(h2[1]);
-      v[0] = a.x; v[1] = a.y; v[2] = c.x; v[3] = c.y;
-    }
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int row0 = tile * kNqRows;
+    const int nrows = min(kNqRows, rows - row0);
+
     if constexpr (NORM) {
-      const float4 wv = __ldg(reinterpret_cast<const float4*>(w + col));
-      const uint2 sc = __ldg(reinterpret_cast<const uint2*>(scale + (int64_t)b * K + col));
-      const uint2 sh = __ldg(reinterpret_cast<const uint2*>(shift + (int64_t)b * K + col));
-      const __nv_bfloat162* sc2 = reinterpret_cast<const __nv_bfloat162*>(&sc);
-      const __nv_bfloat162* sh2 = reinterpret_cast<const __nv_bfloat162*>(&sh);
-      const float ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      float scf[4], shf[4];
-      {
-        float2 a = __bfloat1622float2(sc2[0]), c = __bfloat1622float2(sc2[1]);
-        scf[0] = a.x; scf[1] = a.y; scf[2] = c.x; scf[3] = c.y;
-        a = __bfloat1622float2(sh2[0]); c = __bfloat1622float2(sh2[1]);
-        shf[0] = a.x; shf[1] = a.y; shf[2] = c.x; shf[3] = c.y;
+      // ---- stage A: inverse RMS of each row, reference reduction order
+      for (int r = warp; r < nrows; r += 4) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)(row0 + r) * K) + 2 * lane;
+        float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
+#pragma unroll 4
+        for (int i = 0; i < slabs; ++i) {
+          const uint4 a = __ldg(xr + 64 * i), b = __ldg(xr + 64 * i + 1);
+          // chains: lane 4l+c <- words 2c, 2c+1 of (a, b), low half first.
+          // fma.rn.f32.bf16 widens its bf16 operands exactly, so each step is
+          // fmaf(x, x, sum) of the reference.
+          const uint32_t ws[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float& acc = c == 0 ? s01.x : c == 1 ? s01.y : c == 2 ? s23.x : s23.y;
+            asm("{.reg .b16 l0, h0, l1, h1;\n\t"
+                "mov.b32 {l0, h0}, %1;\n\t"
+                "mov.b32 {l1, h1}, %2;\n\t"
+                "fma.rn.f32.bf16 %0, l0, l0, %0;\n\t"
+                "fma.rn.f32.bf16 %0, h0, h0, %0;\n\t"
+                "fma.rn.f32.bf16 %0, l1, l1, %0;\n\t"
+                "fma.rn.f32.bf16 %0, h1, h1, %0;}"
+                : "+f"(acc)
+                : "r"(ws[2 * c]), "r"(ws[2 * c + 1]));
+          }
+        }
+        float c0 = s01.x, c1 = s01.y, c2 = s23.x, c3 = s23.y;
+        // reference offsets 16, 8, 4 = lanes +4, +2, +1 within 8-lane segments
+#pragma unroll
+        for (int d = 4; d; d >>= 1) {
+          c0 = __fadd_rn(c0, __shfl_down_sync(0xffffffffu, c0, d, 8));
+          c1 = __fadd_rn(c1, __shfl_down_sync(0xffffffffu, c1, d, 8));
+          c2 = __fadd_rn(c2, __shfl_down_sync(0xffffffffu, c2, d, 8));
+          c3 = __fadd_rn(c3, __shfl_down_sync(0xffffffffu, c3, d, 8));
+        }
+        c0 = __fadd_rn(c0, c2);  // offset 2
+        c1 = __fadd_rn(c1, c3);
+        c0 = __fadd_rn(c0, c1);  // offset 1
+        const float w0 = __shfl_sync(0xffffffffu, c0, 0), w1 = __shfl_sync(0xffffffffu, c0, 8);
+        const float w2 = __shfl_sync(0xffffffffu, c0, 16), w3 = __shfl_sync(0xffffffffu, c0, 24);
+        const float total = __fadd_rn(__fadd_rn(w2, w0), __fadd_rn(w3, w1));
+        if (lane == 0) {
+          s_inv[r] = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), eps));
+          const int row = row0 + r;
+          int bb = row / length;
+          if (cut >= 0 && row % length >= cut) bb += batch;
+          s_lat[r] = bb;
+        }
       }
+      __syncthreads();
+    }
+
+    // ---- stage B: modulation + rotation + quantisation, column-stationary
+    for (int i = warp; i < slabs; i += 4) {
+      const int col = 512 * i + 16 * lane;
+      float2 w1[8];
+      uint32_t fm[8], sh[8];
+      int bcur = -1;
+      if constexpr (NORM) {
+        const float4* wp = reinterpret_cast<const float4*>(w + col);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float y = bf16_round(__fmul_rn(__fmul_rn(v[j], inv), __fadd_rn(ww[j], 1.0f)));
-        const float f = bf16_round(__fadd_rn(scf[j], 1.0f));
-        y = bf16_round(__fmul_rn(y, f));
-        v[j] = bf16_round(__fadd_rn(y, shf[j]));
+        for (int k = 0; k < 4; ++k) {
+          const float4 t = __ldg(wp + k);
+          w1[2 * k] = __fadd2_rn(make_float2(t.x, t.y), make_float2(1.0f, 1.0f));
+          w1[2 * k + 1] = __fadd2_rn(make_float2(t.z, t.w), make_float2(1.0f, 1.0f));
+        }
+      }
+      const int kv = K >> 3;  // uint4 per row
+      const uint4* xc = reinterpret_cast<const uint4*>(x + (int64_t)row0 * K + col);
+      // one row: x words (xa, xb) -> codes at qp, scale at sp
+      auto row_body = [&](const uint4 xa, const uint4 xb, int r, uint8_t* qp, __half* sp) {
+        uint32_t vw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        if constexpr (NORM) {
+          const int bb = s_lat[r];
+          if (bb != bcur) {  // warp-uniform: every lane works on the same row
+            bcur = bb;
+            const uint4* cp = reinterpret_cast<const uint4*>(scale + (int64_t)bb * K + col);
+            const uint4* hp = reinterpret_cast<const uint4*>(shift + (int64_t)bb * K + col);
+            const uint4 s0 = __ldg(cp), s1 = __ldg(cp + 1), h0 = __ldg(hp), h1 = __ldg(hp + 1);
+            const uint32_t sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            const uint32_t hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const __nv_bfloat162 one = __floats2bfloat162_rn(1.0f, 1.0f);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              fm[k] = bf2_bits(__hadd2_rn(bf2_from(sv[k]), one));  // bf16(scale + 1)
+              sh[k] = hv[k];
+            }
+          }
+          const float inv = s_inv[r];
+          const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            // y = bf16((x*inv)*(w+1)); y = bf16(y*f); v = bf16(y + shift).  The last
+            // two are bf16x2 ops: a bf16-by-bf16 product or sum rounded once to
+            // bf16 equals its fp32 result rounded to bf16 (fp32 carries more than
+            // 2*8+2 bits), which is the reference's fp32-then-bf16 rounding.  The
+            // .rn forms keep the compiler from contracting them into one fma.
+            const float2 t = __fmul2_rn(__fmul2_rn(bf2_unpack(vw[k]), inv2), w1[k]);
+            const __nv_bfloat162 y = __hmul2_rn(__float22bfloat162_rn(t), bf2_from(fm[k]));
+            vw[k] = bf2_bits(__hadd2_rn(y, bf2_from(sh[k])));
+          }
+        }
+        // layout A: p[k] = (x[2k], x[2k+1]) of this lane's 16 columns
+        float2 p[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) p[k] = bf2_unpack(vw[k]);
+#pragma unroll
+        for (int lk = 0; lk < 3; ++lk) {  // h = 2, 4, 8
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (!(k & (1 << lk))) bfly2(p[k], p[k | (1 << lk)]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<float4*>(tra + 4 * k) =
+              make_float4(p[2 * k].x, p[2 * k].y, p[2 * k + 1].x, p[2 * k + 1].y);
+        __syncwarp();
+        // layout B: o[m] = (x[e], x[e+1]), e = 2v + 16m
+        float2 o[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          o[m] = *reinterpret_cast<const float2*>(trb + 4 * (4 * m + (m >> 1)));
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {  // h = 1
+          const float a = o[m].x, b = o[m].y;
+          o[m] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
+        }
+#pragma unroll
+        for (int lm = 0; lm < 3; ++lm) {  // h = 16, 32, 64
+#pragma unroll
+          for (int m = 0; m < 8; ++m)
+            if (!(m & (1 << lm))) bfly2(o[m], o[m | (1 << lm)]);
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) amax = fmax3(amax, fabsf(o[m].x), fabsf(o[m].y));
+#pragma unroll
+        for (int d = 1; d < 8; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+        const QuantGroup qg = quant_scale(amax);
+        const float c = quant_c_table(qg.sd, s_rcp);
+        const bool clamp = __any_sync(0xffffffffu, qg.clamp);
+        const float2 c2 = make_float2(c, c), mg = make_float2(kRoundMagic8, kRoundMagic8);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          float2 r2 = __ffma2_rn(o[m], c2, mg);
+          if (clamp) {
+            r2.x = fminf(fmaxf(r2.x, kRoundMagic), kRoundMagic + 15.0f);
+            r2.y = fminf(fmaxf(r2.y, kRoundMagic), kRoundMagic + 15.0f);
+          }
+          // low byte = offset-8 nibbles (even element low); bits 4..21 of
+          // each word are zero, so the shifted add carries nothing into it
+          cb[cpos + v + 8 * m] = (uint8_t)((__float_as_uint(r2.y) << 4) + __float_as_uint(r2.x));
+        }
+        __syncwarp();
+        uint2 packed = *reinterpret_cast<const uint2*>(cb + cpos + 8 * v);
+        packed.x ^= 0x88888888u;  // offset-8 -> two's-complement nibbles
+        packed.y ^= 0x88888888u;
+        *reinterpret_cast<uint2*>(qp) = packed;
+        if (v == 0) *sp = qg.scale;
+      };
+      // Two x buffers alternate (row r in A, r+1 in B); each is refilled as
+      // soon as its row is consumed, a row ahead, with no register copies.
+      uint4 a0 = __ldg(xc), a1 = __ldg(xc + 1), b0 = a0, b1 = a1;
+      if (nrows > 1) {
+        b0 = __ldg(xc + kv);
+        b1 = __ldg(xc + kv + 1);
+      }
+      uint8_t* qp = q + (int64_t)row0 * (K >> 1) + 256 * i + 8 * lane;
+      __half* sp = s + (int64_t)row0 * (K >> 7) + 4 * i + g;
+      const uint4* xn = xc + 2 * kv;
+      for (int r = 0; r < nrows; r += 2, qp += K, sp += 2 * (K >> 7), xn += 2 * kv) {
+        row_body(a0, a1, r, qp, sp);
+        if (r + 2 < nrows) {
+          a0 = __ldg(xn);
+          a1 = __ldg(xn + 1);
+        }
+        if (r + 1 < nrows) {
+          row_body(b0, b1, r + 1, qp + (K >> 1), sp + (K >> 7));
+          if (r + 3 < nrows) {
+            b0 = __ldg(xn + kv);
+            b1 = __ldg(xn + kv + 1);
+          }
+        }
       }
     }
-    // Sylvester H128, stages h = 1, 2 in registers ...
-    {
-      const float a0 = __fadd_rn(v[0], v[1]), a1 = __fsub_rn(v[0], v[1]);
-      const float a2 = __fadd_rn(v[2], v[3]), a3 = __fsub_rn(v[2], v[3]);
-      v[0] = __fadd_rn(a0, a2); v[2] = __fsub_rn(a0, a2);
-      v[1] = __fadd_rn(a1, a3); v[3] = __fsub_rn(a1, a3);
-    }
-    // ... h = 4 .. 64 across lanes (partner = lane ^ h/4).
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-      const bool upper = (lane & m) != 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
-        v[j] = upper ? __fsub_rn(o, v[j]) : __fadd_rn(v[j], o);
-      }
-    }
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[j] = __fmul_rn(v[j], kHadamardScale);
-      amax = fmaxf(amax, fabsf(v[j]));
-    }
-#pragma unroll
-    for (int m = 16; m; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-    const __half hs = group_scale(amax);
-    const float sd = __half2float(hs);
-    const int gidx = 4 * i + warp;
-    if (lane == 0) sr[gidx] = hs;
-    uint32_t packed = 0;
-    if (sd > 0.0f) {
-      const float rcp = __frcp_rn(sd);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) packed |= (uint32_t)(quant_code(v[j], sd, rcp) & 0xF) << (4 * j);
-    }
-    reinterpret_cast<uint16_t*>(qr + gidx * 64)[lane] = (uint16_t)packed;
+    __syncthreads();  // s_inv is rewritten by the next tile's stage A
   }
 }
 

@@ -6,9 +6,10 @@
  * and only as the checker.
  *
  * Every function states the reference code it restates (paths are relative to
- * the ComfyUI-K2-Precompile project).  Where BASELINE's contract differs from
- * the reference (group-128 fp16 scales, normalised H128 rotation, RNE quant),
- * the contract is the one both this file and the CUDA kernels follow; the
+ * the ComfyUI-K2-Precompile project).  Where this project's W4A4 contract
+ * differs from the reference (group-128 fp16 scales, normalised H128
+ * rotation, RNE quant), the contract is the one both this file and the CUDA
+ * kernels follow; the
  * reference's rounding points (bf16 after every modulation step, fp32 fmaf
  * chains) are kept.
  *
@@ -103,44 +104,61 @@ float k2o_sigmoid(float x) { return 1.0f / (1.0f + k2o_exp(-x)); }
 /* fp32(1/sqrt(128)): the normalisation of the Sylvester H128 block. */
 #define K2_HSCALE 0.0883883461356163024902343750f
 
-/* In-place Sylvester Walsh-Hadamard transform of 128 fp32 values, stages
- * h = 1, 2, 4, ..., 64; (a, b) -> (a + b, a - b).  Then scaled by K2_HSCALE.
- * This is the contract's "normalised 128x128 block-Hadamard".
- * The reference rotates with comfy-kitchen's ConvRot stages
- * (kernels/norm_quant.cu:40-60); those helpers are not vendored. */
+/* In-place unnormalised Walsh-Hadamard transform of 128 fp32 values: seven
+ * butterfly stages (a, b) -> (a + b, a - b) between elements h apart, each
+ * sum rounded to fp32, in the order h = 2, 4, 8, 1, 16, 32, 64.  The
+ * 1/sqrt(128) normalisation of the orthonormal 128x128 block-Hadamard is not
+ * applied here: k2o_quant_group128 folds it into the scale and the
+ * per-element multiplier.  The reference rotates with comfy-kitchen's
+ * ConvRot stages (kernels/norm_quant.cu:40-60, helpers not vendored); the
+ * stage order and rounding here are this project's own contract (any order
+ * is the same transform in exact arithmetic). */
+static const int k2o_hadamard_order[7] = {2, 4, 8, 1, 16, 32, 64};
 void k2o_hadamard128(float* v) {
-    for (int h = 1; h < 128; h <<= 1)
+    for (int st = 0; st < 7; ++st) {
+        const int h = k2o_hadamard_order[st];
         for (int i = 0; i < 128; i += 2 * h)
             for (int j = i; j < i + h; ++j) {
                 float a = v[j], b = v[j + h];
                 v[j] = a + b;
                 v[j + h] = a - b;
             }
-    for (int j = 0; j < 128; ++j) v[j] = v[j] * K2_HSCALE;
+    }
 }
 
-/* Quantise one rotated group of 128: scale = fp16(absmax / 7), codes =
- * clamp(rne(v / scale), -8, 7) (correctly rounded division), two codes per
- * byte, low nibble = even column.  Follows the role of kitchen's
- * finite_absmax_for_int4_scale / quantize_int4_pack4_word
- * (kernels/norm_quant.cu:61-66) with BASELINE's group-128 fp16 scale. */
-void k2o_quant_group128(const float* v, uint8_t* q, uint16_t* s) {
+/* Quantise one group of 128 raw Hadamard outputs u (k2o_hadamard128) to
+ * INT4 codes of the normalised rotation u * K2_HSCALE:
+ *   scale = fp16(min(fp32(max|u| * K2_QSCALE), 65504))
+ *           K2_QSCALE = fp32(1/(7*sqrt(128))): absmax of the normalised
+ *           group over the INT4 maximum 7, as one multiply
+ *   c     = fp32(K2_HSCALE * fp32(1 / scale))   (0 for a zero scale)
+ *   code  = clamp(rne(u * c), -8, 7)      (u * c exact: one rounding)
+ * two codes per byte, low nibble = even column.  Multiplying by the
+ * reciprocal of the scale is the reference's quantisation step
+ * (kernels/norm_quant.cu:62-66: inverse = 1.f/row_scale, then
+ * quantize_int4_pack4_word(..., inverse, ...)), here with one fp16 scale per
+ * group of 128.  The rounding is written as fma(u, c, 1.5*2^23): its sum
+ * lies on the integer grid, so it is rne(u*c) + 1.5*2^23 exactly; codes of
+ * NaN inputs are unspecified (the scale ignores them). */
+#define K2_ROUND_MAGIC 12582912.0f
+#define K2_QSCALE 0.012626906856894493103027343750f
+void k2o_quant_group128(const float* u, uint8_t* q, uint16_t* s) {
     float amax = 0.0f;
-    for (int j = 0; j < 128; ++j) amax = fmaxf(amax, fabsf(v[j]));
-    float sf = amax / 7.0f;
+    for (int j = 0; j < 128; ++j) amax = fmaxf(amax, fabsf(u[j]));
+    float sf = amax * K2_QSCALE;
     if (sf > 65504.0f) sf = 65504.0f;
     uint16_t sh = k2o_f32_to_f16(sf);
     float sd = k2o_f16_to_f32(sh);
     *s = sh;
+    float c = sd > 0.0f ? K2_HSCALE * (1.0f / sd) : 0.0f;
     for (int j = 0; j < 128; j += 2) {
-        int c[2];
+        int code[2];
         for (int t = 0; t < 2; ++t) {
-            float r = sd > 0.0f ? rintf(v[j + t] / sd) : 0.0f;
-            if (r > 7.0f) r = 7.0f;
-            if (r < -8.0f) r = -8.0f;
-            c[t] = (int)r;
+            float r = fmaf(u[j + t], c, K2_ROUND_MAGIC);
+            r = fminf(fmaxf(r, K2_ROUND_MAGIC - 8.0f), K2_ROUND_MAGIC + 7.0f);
+            code[t] = (int)(r - K2_ROUND_MAGIC);
         }
-        q[j / 2] = (uint8_t)((c[0] & 0xf) | ((c[1] & 0xf) << 4));
+        q[j / 2] = (uint8_t)((code[0] & 0xf) | ((code[1] & 0xf) << 4));
     }
 }
 
@@ -180,8 +198,8 @@ static int mod_row(int row, int length, int cut, int batch) {
 
 /*
  * Fused RMSNorm -> adaLN modulation -> H128 rotation -> group-128 INT4 pack.
- * Restates kernels/norm_quant.cu:11-67 (norm_mod_quant) with BASELINE's
- * rotation and scale layout:
+ * Restates kernels/norm_quant.cu:11-67 (norm_mod_quant), with the group-128
+ * rotation and fp16 scales of k2o_hadamard128 / k2o_quant_group128:
  *   inv = rsqrt_rn(sum/K + eps)                          (:30-31)
  *   y   = bf16((x*inv)*(w+1))                            (:34)
  *   f   = bf16(scale+1); y = bf16(y*f); v = bf16(y+shift) (:35-37)
@@ -241,7 +259,7 @@ int k2o_norm_mod(const uint16_t* x, const float* w, const uint16_t* scale, const
 
 /* Rotation + quantisation of an already-formed bf16 activation (the input
  * quantisation that native_runtime.cpp:268-271 `quantize` performs before the
- * out-projection), BASELINE contract. */
+ * out-projection), with the group-128 rotation and scales above. */
 int k2o_rotate_quant(const uint16_t* x, uint8_t* q, uint16_t* s, int rows, int K) {
     if (rows <= 0 || K <= 0 || K % 128) return 1;
     for (int row = 0; row < rows; ++row) {
