@@ -7,18 +7,34 @@
 // ResidualGemm (kernels/int4_epilogue.cu:18-66) and QKGemm + NormRopeStore
 // (kernels/qk_norm_rope.cu:19-133).
 //
-// Tile: 128 rows (M) x 256 columns (N) per CTA, K consumed one 128-wide
-// quantisation group per pipeline stage.  Roles (640 threads):
-//   warp 0      TMA producer: packed A group tile (128 x 64 B), prepared W
-//               group tile (256 x 128 B, 128B-swizzled), W group scales (1 KB)
-//   warp 1      TMEM allocator + single-thread MMA issuer (4 x K=32 MMAs per group)
+// Tile: a CTA pair (cluster of 2 along M) computes 256 rows x 256 columns;
+// each CTA owns 128 rows of A and holds half of the W tile (128 of the 256
+// columns; for SwiGLU the leader holds the gate rows, the peer the up rows).
+// The leader issues tcgen05.mma.cta_group::2 (M = 256, N = 256): the tensor
+// cores of both SMs read A from their own CTA and B from both, so each SM
+// streams 16 KB of A + 16 KB of W per 128-wide K group instead of 16 + 32
+// (a single-CTA M = 128 MMA measured ~740 cycles per group against ~400 for
+// the pair).  K is consumed one quantisation group per pipeline stage.
+// Roles (640 threads per CTA):
+//   warp 0      TMA producer: packed A group tile (128 x 64 B), this CTA's
+//               half of the prepared W group tile (128 x 128 B, 128B-swizzled);
+//               W scales of all 256 columns in chunks of 16 groups (16 KB)
+//   warp 1      TMEM allocator (both CTAs, cta_group::2); leader: single-thread
+//               MMA issuer (4 x K=32 MMAs per group); peer: relays "stage
+//               ready" (W landed + A unpacked) to the leader
 //   warps 2-3   A unpackers: s4 -> s8 (x16) into the 128B-swizzled UMMA layout
 //   warps 4-19  epilogue: TMEM lane quadrant = warp % 4, column quarter
 //               = (warp-4)/4 (64 columns of one row per thread)
+// Stage barrier full_s[s] collects this CTA's W bytes (producer expect_tx),
+// its two unpacker arrivals and, on the leader, the peer's relay.  MMA
+// completion is committed to the same barrier offset in both CTAs (multicast
+// commit); the peer's relay and its epilogue warps arrive on the leader's
+// barriers remotely.  TMA copies complete on local barriers only, so each CTA
+// can drain its own copies.
 // TMEM: 2 x 256 int32 columns, one per group in flight (ping-pong), so the MMA
 // of group g+1 overlaps the dequant of group g.  The fp32 group sum lives in
-// the epilogue registers (64 per thread); four epilogue warps per scheduler
-// hide the TMEM load latency.  setmaxnreg gives the TMA/MMA/unpack warpgroup
+// the epilogue registers (64 per thread); TMEM loads are software-pipelined
+// one 16-column chunk ahead.  setmaxnreg gives the TMA/MMA/unpack warpgroup
 // 32 registers and the four epilogue warpgroups 112.
 //
 // Dequant contract (oracle: k2o_gemm_w4a4):
@@ -37,7 +53,7 @@ namespace k2b {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
-constexpr int GEMM_STAGES = 3;   // prepared W + unpacked A
+constexpr int GEMM_STAGES = 4;   // prepared W half + unpacked A
 constexpr int GEMM_PSTAGES = 4;  // packed A and W scales
 constexpr int GEMM_EPI_WARPS = 16;
 constexpr int GEMM_THREADS = 128 + 32 * GEMM_EPI_WARPS;  // 640
@@ -47,17 +63,21 @@ constexpr int GEMM_THREADS = 128 + 32 * GEMM_EPI_WARPS;  // 640
 // any other allocation.
 constexpr int GEMM_LAUNCH_REGS = 96;
 
-constexpr int GEMM_W_BYTES = GEMM_BN * 128;       // 32 KB
+constexpr int GEMM_W_BYTES = GEMM_BN / 2 * 128;   // 16 KB: this CTA's half of the W tile
 constexpr int GEMM_UA_BYTES = GEMM_BM * 128;      // 16 KB
 constexpr int GEMM_PA_BYTES = GEMM_BM * 64;       // 8 KB
-constexpr int GEMM_SC_BYTES = GEMM_BN * 4;        // 1 KB
+constexpr int GEMM_SC_GROUPS = 16;                // W scales arrive in chunks of 16 K groups
+constexpr int GEMM_SC_BYTES = GEMM_BN * 4 * GEMM_SC_GROUPS;  // 16 KB per chunk, two chunk buffers
 constexpr int GEMM_OFF_W = 0;
 constexpr int GEMM_OFF_UA = GEMM_OFF_W + GEMM_STAGES * GEMM_W_BYTES;
 constexpr int GEMM_OFF_PA = GEMM_OFF_UA + GEMM_STAGES * GEMM_UA_BYTES;
 constexpr int GEMM_OFF_SC = GEMM_OFF_PA + GEMM_PSTAGES * GEMM_PA_BYTES;
-constexpr int GEMM_OFF_BAR = GEMM_OFF_SC + GEMM_PSTAGES * GEMM_SC_BYTES;
-constexpr int GEMM_NBARS = 3 * GEMM_STAGES + 4 * GEMM_PSTAGES + 4;
+constexpr int GEMM_OFF_BAR = GEMM_OFF_SC + 2 * GEMM_SC_BYTES;
+constexpr int GEMM_NBARS = 2 * GEMM_STAGES + 2 * GEMM_PSTAGES + 2 * 2 + 4;
 constexpr int GEMM_SMEM_BYTES = GEMM_OFF_BAR + GEMM_NBARS * 8 + 16 + 1024;  // + alignment slack
+// The final epilogue exchanges rows through the (then idle) W, unpacked-A and
+// packed-A stages: SwiGLU needs 2*128*65 + 2*128*66 floats.
+static_assert(GEMM_OFF_SC >= (2 * 128 * 65 + 2 * 128 * 66) * 4, "exchange space");
 // Accumulator seed: as fp32 bits, 0x4B400000 + x reads as 12582912 + x for |x| < 2^22.
 constexpr uint32_t kAccBias = 0x4B400000u;
 
@@ -143,19 +163,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GEMM_OFF_BAR);
-  uint64_t* full_w = bars;                          // [STAGES] TMA W landed
-  uint64_t* full_ua = full_w + GEMM_STAGES;         // [STAGES] A unpacked
-  uint64_t* empty_s = full_ua + GEMM_STAGES;        // [STAGES] MMAs done with W/A stage
+  // full_s[s]: this CTA's W half landed (producer's expect_tx arrival + TMA
+  // bytes) and its A unpacked (2 unpacker arrivals); on the leader also the
+  // peer's stage (1 arrival relayed by the peer).
+  uint64_t* full_s = bars;                          // [STAGES]
+  uint64_t* empty_s = full_s + GEMM_STAGES;         // [STAGES] MMAs done with W/A stage (both CTAs)
   uint64_t* full_pa = empty_s + GEMM_STAGES;        // [PSTAGES] TMA packed A landed
   uint64_t* empty_pa = full_pa + GEMM_PSTAGES;      // [PSTAGES] unpackers done
-  uint64_t* full_sc = empty_pa + GEMM_PSTAGES;      // [PSTAGES] W scales landed
-  uint64_t* empty_sc = full_sc + GEMM_PSTAGES;      // [PSTAGES] epilogue done with scales
-  uint64_t* tmem_full = empty_sc + GEMM_PSTAGES;    // [2] MMAs of a group done
-  uint64_t* tmem_empty = tmem_full + 2;             // [2] buffer drained
+  uint64_t* full_sc = empty_pa + GEMM_PSTAGES;      // [2] W scale chunk landed
+  uint64_t* empty_sc = full_sc + 2;                 // [2] epilogue done with a scale chunk
+  uint64_t* tmem_full = empty_sc + 2;               // [2] MMAs of a group done (both CTAs)
+  uint64_t* tmem_empty = tmem_full + 2;             // [2] leader: buffer drained by both CTAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + GEMM_NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: leader (issues the pair's MMAs), 1: peer
+  const bool leader = rank == 0;
   const int m0 = blockIdx.x * GEMM_BM;
   // Segment of this N tile.
   int seg = 0, tile = blockIdx.y;
@@ -171,26 +195,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < GEMM_STAGES; ++i) {
-      mbar_init(&full_w[i], 1);
-      mbar_init(&full_ua[i], 2);
+      mbar_init(&full_s[i], leader ? 4 : 3);
       mbar_init(&empty_s[i], 1);
     }
     for (int i = 0; i < GEMM_PSTAGES; ++i) {
       mbar_init(&full_pa[i], 1);
       mbar_init(&empty_pa[i], 2);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&full_sc[i], 1);
       mbar_init(&empty_sc[i], GEMM_EPI_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tmem_full[i], 1);
-      mbar_init(&tmem_empty[i], GEMM_EPI_WARPS);
+      mbar_init(&tmem_empty[i], 2 * GEMM_EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // Both CTAs' barriers are initialised before either CTA signals the other.
+  cluster_sync_all();
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
@@ -203,48 +230,58 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 0) {
       // ----------------------------------------------------- TMA producer
       if (lane == 0) {
-        const CUtensorMap* wmap = &wmaps.m[pairw ? 0 : seg];
+        const CUtensorMap* wmap = &wmaps.m[pairw ? rank : seg];
+        const int wrow = pairw ? n0 : n0 + 128 * (int)rank;
         for (int g = 0; g < G; ++g) {
           const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
           const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
           if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&full_w[s], GEMM_W_BYTES);
-          if (pairw) {
-            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, &wmaps.m[0], &full_w[s], g * 128, n0);
-            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES + GEMM_W_BYTES / 2, &wmaps.m[1], &full_w[s], g * 128,
-                        n0);
-          } else {
-            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_w[s], g * 128, n0);
-          }
+          mbar_arrive_expect_tx(&full_s[s], GEMM_W_BYTES);
+          // this CTA's 128 of the pair's 256 B columns (SwiGLU: gate | up)
+          tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_s[s], g * 128, wrow);
           issued_w = g + 1;
           if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pa[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
           mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
           tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
           issued_pa = g + 1;
-          if (g >= GEMM_PSTAGES && !mbar_wait(&empty_sc[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&full_sc[ps], GEMM_SC_BYTES);
-          if (pairw) {
-            bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES, S.wscale + (int64_t)g * S.n + n0, GEMM_SC_BYTES / 2,
-                      &full_sc[ps]);
-            bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES + GEMM_SC_BYTES / 2, S.wscale2 + (int64_t)g * S.n + n0,
-                      GEMM_SC_BYTES / 2, &full_sc[ps]);
-          } else {
-            bulk_load(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES, S.wscale + (int64_t)g * S.n + n0, GEMM_SC_BYTES,
-                      &full_sc[ps]);
+          // Scale chunk c (groups 16c .. 16c+15) goes to buffer c % 2: chunks 0
+          // and 1 at the start, chunk c+1 once the producer is 8 groups into
+          // chunk c (the epilogue has then released chunk c-1).
+          const int nchunks = (G + GEMM_SC_GROUPS - 1) / GEMM_SC_GROUPS;
+          int chunk = -1;
+          if (g == 0) chunk = 0;
+          else if (g == 1 && nchunks > 1) chunk = 1;
+          else if (g % GEMM_SC_GROUPS == GEMM_SC_GROUPS / 2 && g / GEMM_SC_GROUPS + 1 < nchunks && g >= GEMM_SC_GROUPS)
+            chunk = g / GEMM_SC_GROUPS + 1;
+          if (chunk >= 0) {
+            const int cb = chunk & 1;
+            if (chunk >= 2 && !mbar_wait(&empty_sc[cb], ((chunk >> 1) & 1) ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+            const int g0 = chunk * GEMM_SC_GROUPS;
+            const int ng = min(GEMM_SC_GROUPS, G - g0);
+            mbar_arrive_expect_tx(&full_sc[cb], ng * GEMM_BN * 4);
+            uint8_t* dst = smem + GEMM_OFF_SC + cb * GEMM_SC_BYTES;
+            for (int j = 0; j < ng; ++j) {
+              const int64_t off = (int64_t)(g0 + j) * S.n + n0;
+              if (pairw) {
+                bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 2, &full_sc[cb]);
+                bulk_load(dst + j * GEMM_BN * 4 + GEMM_BN * 2, S.wscale2 + off, GEMM_BN * 2, &full_sc[cb]);
+              } else {
+                bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 4, &full_sc[cb]);
+              }
+            }
+            issued_sc = chunk + 1;
           }
-          issued_sc = g + 1;
         }
       }
     } else if (warp == 1) {
-      // ----------------------------------------------------- MMA issuer
-      if (lane == 0) {
-        constexpr uint32_t idesc = make_idesc(2, 1, 1, 0, 0, GEMM_BM, GEMM_BN);
+      // ------------------------------------- MMA issuer (leader) / relay (peer)
+      if (lane == 0 && leader) {
+        constexpr uint32_t idesc = make_idesc(2, 1, 1, 0, 0, 2 * GEMM_BM, GEMM_BN);
         for (int g = 0; g < G; ++g) {
           const int s = g % GEMM_STAGES, b = g & 1;
           const uint32_t ph = (g / GEMM_STAGES) & 1, bph = (g >> 1) & 1;
-          if (!mbar_wait(&full_w[s], ph, abort_flag, ERR_WAIT_MMA)) break;
-          if (!mbar_wait(&full_ua[s], ph, abort_flag, ERR_WAIT_MMA)) break;
-          if (g >= 2 && !mbar_wait(&tmem_empty[b], bph ^ 1, abort_flag, ERR_WAIT_MMA)) break;
+          if (!mbar_wait_cluster(&full_s[s], ph, abort_flag, ERR_WAIT_MMA)) break;
+          if (g >= 2 && !mbar_wait_cluster(&tmem_empty[b], bph ^ 1, abort_flag, ERR_WAIT_MMA)) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES);
           const uint32_t w_base = smem_u32(smem + GEMM_OFF_W + s * GEMM_W_BYTES);
@@ -252,11 +289,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = umma_desc_sw128(a_base + 32 * k, 16, 1024);
             const uint64_t bd = umma_desc_sw128(w_base + 32 * k, 16, 1024);
-            mma_i8_ss(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
+            mma_i8_pair(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
           }
-          mma_commit(&empty_s[s]);
-          mma_commit(&tmem_full[b]);
+          mma_commit_pair(&empty_s[s]);
+          mma_commit_pair(&tmem_full[b]);
           issued_mma = g + 1;
+        }
+      } else if (lane == 0) {
+        // the peer's W half has landed and its A is unpacked: tell the leader
+        const uint32_t ready0 = cluster_map(smem_u32(&full_s[0]), 0);
+        for (int g = 0; g < G; ++g) {
+          const int s = g % GEMM_STAGES;
+          const uint32_t ph = (g / GEMM_STAGES) & 1;
+          if (!mbar_wait(&full_s[s], ph, abort_flag, ERR_WAIT_MMA)) break;
+          mbar_arrive_remote(ready0 + 8u * (uint32_t)s);
         }
       }
     } else {
@@ -290,7 +336,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&empty_pa[ps]);
-          mbar_arrive(&full_ua[s]);
+          mbar_arrive(&full_s[s]);
         }
       }
     }
@@ -304,48 +350,82 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const bool row_ok = row < p.M;
     const __half* sa_row = p.sa + (int64_t)(row_ok ? row : 0) * G;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + cq * 64;
+    const uint32_t tmem_empty_remote = cluster_map(smem_u32(tmem_empty), 0);
     bool ok = true;
     float2 acc2[32];  // columns (2j, 2j+1)
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc2[j] = make_float2(0.0f, 0.0f);
+    // TMEM loads are software-pipelined: the load of chunk c+1 (16 columns)
+    // is in flight while chunk c is dequantised, and the first load of group
+    // g+1 overlaps the last chunk of group g.  Barriers, scales and the abort
+    // flag are addressed with 32-bit shared addresses to leave the registers
+    // to the accumulators and the two load buffers.
+    const uint32_t s_full_sc = smem_u32(full_sc), s_empty_sc = smem_u32(empty_sc);
+    const uint32_t s_tfull = smem_u32(tmem_full), s_tempty = smem_u32(tmem_empty);
+    const uint32_t s_abort = smem_u32((const void*)abort_flag);
+    const uint32_t s_scales = smem_u32(smem + GEMM_OFF_SC) + cq * 64 * 4;
+    auto dequant16 = [&](const uint32_t (&v)[16], uint32_t scs, int c0, float2 sa2, float2 sb2) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 sw = lds128(scs + 4 * (c0 + i));  // scales of columns c0+i .. +3
+        const float2 u0 = __ffma2_rn(
+            make_float2(__uint_as_float(v[i] + kAccBias), __uint_as_float(v[i + 1] + kAccBias)), sa2, sb2);
+        const float2 u1 = __ffma2_rn(
+            make_float2(__uint_as_float(v[i + 2] + kAccBias), __uint_as_float(v[i + 3] + kAccBias)), sa2, sb2);
+        acc2[(c0 + i) / 2] = __ffma2_rn(u0, make_float2(sw.x, sw.y), acc2[(c0 + i) / 2]);
+        acc2[(c0 + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(c0 + i) / 2 + 1]);
+      }
+    };
+    uint32_t va[16], vb[16];
+    ok = mbar_wait_s(s_full_sc, 0, s_abort, ERR_WAIT_EPILOGUE) && mbar_wait_s(s_tfull, 0, s_abort, ERR_WAIT_EPILOGUE);
+    if (ok) {
+      tc_fence_after();
+      tmem_ld16(lane_base, va);
+    }
     __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
     for (int g = 0; g < G && ok; ++g) {
-      const int b = g & 1, ps = g % GEMM_PSTAGES;
-      const uint32_t bph = (g >> 1) & 1, pph = (g / GEMM_PSTAGES) & 1;
+      const int b = g & 1, cb = (g / GEMM_SC_GROUPS) & 1;
       const float sa = row_ok ? __fmul_rn(__half2float(sa_next), 0.00390625f) : 0.0f;
       if (g + 1 < G) sa_next = sa_row[g + 1];
       const float sbias = __fmul_rn(sa, -12582912.0f);
       const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sbias, sbias);
-      if (!mbar_wait(&full_sc[ps], pph, abort_flag, ERR_WAIT_EPILOGUE)) { ok = false; break; }
-      if (!mbar_wait(&tmem_full[b], bph, abort_flag, ERR_WAIT_EPILOGUE)) { ok = false; break; }
-      tc_fence_after();
-      const float4* scs = reinterpret_cast<const float4*>(smem + GEMM_OFF_SC + ps * GEMM_SC_BYTES + cq * 64 * 4);
+      const uint32_t scs = s_scales + cb * GEMM_SC_BYTES + (g % GEMM_SC_GROUPS) * GEMM_BN * 4;
       const uint32_t taddr = lane_base + b * GEMM_BN;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[16];
-        tmem_ld16(taddr + 16 * c, v);
-        tmem_wait_ld_regs(v);
-        if (c == 3) {
-          // every column is in registers: hand the buffer back to the MMA
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tmem_empty[b]);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 sw = scs[(16 * c + i) / 4];  // scales of columns 16c+i .. +3
-          const float2 u0 = __ffma2_rn(
-              make_float2(__uint_as_float(v[i] + kAccBias), __uint_as_float(v[i + 1] + kAccBias)), sa2, sb2);
-          const float2 u1 = __ffma2_rn(
-              make_float2(__uint_as_float(v[i + 2] + kAccBias), __uint_as_float(v[i + 3] + kAccBias)), sa2, sb2);
-          acc2[(16 * c + i) / 2] = __ffma2_rn(u0, make_float2(sw.x, sw.y), acc2[(16 * c + i) / 2]);
-          acc2[(16 * c + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(16 * c + i) / 2 + 1]);
+      tmem_wait_ld_regs(va);
+      tmem_ld16(taddr + 16, vb);
+      dequant16(va, scs, 0, sa2, sb2);
+      tmem_wait_ld_regs(vb);
+      tmem_ld16(taddr + 32, va);
+      dequant16(vb, scs, 16, sa2, sb2);
+      tmem_wait_ld_regs(va);
+      tmem_ld16(taddr + 48, vb);
+      dequant16(va, scs, 32, sa2, sb2);
+      tmem_wait_ld_regs(vb);
+      // every column of group g is in registers: hand the buffer back to the MMA
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive_s(s_tempty + 8u * (uint32_t)b);
+        else mbar_arrive_remote(tmem_empty_remote + 8u * (uint32_t)b);
+      }
+      if (g + 1 < G) {
+        const int g1 = g + 1;
+        const int c1 = g1 / GEMM_SC_GROUPS;
+        if ((g1 % GEMM_SC_GROUPS != 0 ||
+             mbar_wait_s(s_full_sc + 8u * (uint32_t)(c1 & 1), (c1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) &&
+            mbar_wait_s(s_tfull + 8u * (uint32_t)(g1 & 1), (g1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) {
+          tc_fence_after();
+          tmem_ld16(lane_base + (g1 & 1) * GEMM_BN, va);
+        } else {
+          ok = false;
         }
       }
+      dequant16(vb, scs, 48, sa2, sb2);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_sc[ps]);
+      if (lane == 0 && (g % GEMM_SC_GROUPS == GEMM_SC_GROUPS - 1 || g == G - 1))
+        mbar_arrive_s(s_empty_sc + 8u * (uint32_t)cb);
     }
+    if (!ok) tmem_wait_ld();  // no TMEM load stays in flight
 
     float acc[64];
 #pragma unroll
@@ -531,12 +611,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (*abort_flag) {
     // let copies and MMAs that were already issued land before the CTA exits
     if (warp == 0 && lane == 0) {
+      // (a stage's full barrier also waits for unpacker arrivals, so only
+      // the transaction bytes are certain: drain with a bounded wait)
       for (int g = (issued_w > GEMM_STAGES ? issued_w - GEMM_STAGES : 0); g < issued_w; ++g)
-        mbar_drain(&full_w[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
+        mbar_drain(&full_s[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
       for (int g = (issued_pa > GEMM_PSTAGES ? issued_pa - GEMM_PSTAGES : 0); g < issued_pa; ++g)
         mbar_drain(&full_pa[g % GEMM_PSTAGES], (g / GEMM_PSTAGES) & 1);
-      for (int g = (issued_sc > GEMM_PSTAGES ? issued_sc - GEMM_PSTAGES : 0); g < issued_sc; ++g)
-        mbar_drain(&full_sc[g % GEMM_PSTAGES], (g / GEMM_PSTAGES) & 1);
+      for (int c = (issued_sc > 2 ? issued_sc - 2 : 0); c < issued_sc; ++c)
+        mbar_drain(&full_sc[c & 1], (c >> 1) & 1);
     }
     if (warp == 1 && lane == 0 && issued_mma > 0) {
       const int g = issued_mma - 1;
@@ -545,9 +627,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // The leader's MMAs (which read the peer's shared memory) are complete and
+  // no arrival from one CTA to the other is in flight once both get here.
+  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 

@@ -68,22 +68,83 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes or
+// `hint_ns` elapses: a waiting warp then issues nothing, instead of polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kWaitSleepNs = 1000000;  // 1 ms per suspension
+
 // Bounded wait for the completion of phase `parity` of `bar`.  Returns false
 // (after raising *abort and recording `code`) if the CTA was aborted or the
-// wait exceeded kWaitLimitNs.
+// wait exceeded kWaitLimitNs.  Between checks the thread sleeps in
+// try_wait (woken by the phase completing), so waiting warps leave the issue
+// slots to the warps doing work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = global_timer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((i & 15u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicOr(&g_error, code);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(a, parity, kWaitSleepNs)) return true;
+    if (*abort_flag) return false;
+    if (global_timer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicOr(&g_error, code);
+      return false;
+    }
+  }
+}
+
+// mbar_wait on 32-bit shared-memory addresses (barrier and abort flag), for
+// loops that cannot spare registers for generic pointers.
+__device__ __forceinline__ bool mbar_wait_s(uint32_t a, uint32_t parity, uint32_t abort_addr, int code) {
+  if (mbar_try_wait(a, parity)) return true;
+  const unsigned long long t0 = global_timer();
+  for (;;) {
+    if (mbar_try_wait_sleep(a, parity, kWaitSleepNs)) return true;
+    int ab;
+    asm volatile("ld.volatile.shared.b32 %0, [%1];" : "=r"(ab) : "r"(abort_addr) : "memory");
+    if (ab) return false;
+    if (global_timer() - t0 > kWaitLimitNs) {
+      asm volatile("st.volatile.shared.b32 [%0], %1;" ::"r"(abort_addr), "r"(1) : "memory");
+      atomicOr(&g_error, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void mbar_arrive_s(uint32_t a) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ float4 lds128(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+
+// mbar_wait for phases completed by arrivals from the other CTA of the pair.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  const uint32_t a = smem_u32(bar);
+  const unsigned long long t0 = global_timer();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity), "r"(kWaitSleepNs)
+        : "memory");
+    if (ok) return true;
+    if (*abort_flag) return false;
+    if (global_timer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicOr(&g_error, code);
+      return false;
     }
   }
 }
@@ -136,6 +197,59 @@ __device__ __forceinline__ void tmem_relinquish() {
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// ---- CTA pair (cluster of 2) forms: the pair shares one MMA issued by
+// cluster rank 0; TMEM is allocated at the same columns in both CTAs.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of this CTA's shared-memory word `addr` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of another CTA of the cluster (cluster_map address).
+// Default (release) semantics, as the CTA-pair pipelines of CUTLASS use: a
+// cluster-scope release here measured ~800 cycles per arrival.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// M = 256 MMA over the pair: A rows 0-127 / 128-255 and B columns 0-N/2-1 /
+// N/2.. from the two CTAs' shared memory at the same offsets; each CTA's TMEM
+// receives its 128 rows.
+__device__ __forceinline__ void mma_i8_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, "
+      "p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Completion of the pair's prior MMAs arrives on the mbarrier at this offset
+// in both CTAs.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

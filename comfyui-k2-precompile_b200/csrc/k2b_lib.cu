@@ -158,13 +158,14 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     if (pairw && nseg != 1) return (int)cudaErrorInvalidValue;
     const int tile_n = pairw ? GEMM_BN / 2 : GEMM_BN;
     if (d.n <= 0 || d.n % tile_n || !aligned16(d.w) || !aligned16(d.wscale) || !d.out) return (int)cudaErrorInvalidValue;
+    // each CTA of a pair loads 128 weight rows per K group
     int rc = make_map_2d(&wm.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w, (uint64_t)K, (uint64_t)d.n, (uint64_t)K,
-                         128, tile_n, CU_TENSOR_MAP_SWIZZLE_128B);
+                         128, GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     if (pairw) {
       if (!aligned16(d.w2) || !aligned16(d.wscale2)) return (int)cudaErrorInvalidValue;
       rc = make_map_2d(&wm.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w2, (uint64_t)K, (uint64_t)d.n, (uint64_t)K, 128,
-                       tile_n, CU_TENSOR_MAP_SWIZZLE_128B);
+                       GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
       if (rc) return rc;
     }
     GemmSegment& g = p.seg[i];
@@ -215,8 +216,22 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     if (fa.numRegs != GEMM_LAUNCH_REGS) return (int)cudaErrorInvalidConfiguration;
     attr_set[dev] = true;
   }
-  dim3 grid((M + GEMM_BM - 1) / GEMM_BM, tiles);
-  gemm_w4a4_kernel<<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(amap, wm, p);
+  // CTA pairs along M (cluster 2 x 1 x 1): 256 rows per pair.
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(2 * ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)), tiles, 1);
+  cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = GEMM_SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_w4a4_kernel, amap, wm, p);
+  if (e != cudaSuccess) return (int)e;
   return launch_status();
 }
 
