@@ -286,6 +286,35 @@ def run_kernel_case(args):
                       "avg_us": s.elapsed_time(e) * 1e3 / args.reps}), flush=True)
 
 
+def run_profile_pass(args):
+    """--profile: the timed step's kernels and nothing else (no peak probe, no
+    end-to-end pass, no CPU baseline): `warmup` forward passes, then one more.
+    Each pass launches 7 kernels per block (28 blocks) after one input copy."""
+    import torch
+
+    from k2b.model import Krea2Blocks, ModelConfig, rope_positions, rope_table, synthetic_blocks
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig()
+    blocks = synthetic_blocks(cfg, LATENTS, seed=1234, device=dev)
+    freqs = rope_table(rope_positions(TEXT, GRID, GRID), (64, 64), cfg.theta).to(dev)
+    model = Krea2Blocks(cfg, blocks, LATENTS, LENGTH, device=dev)
+    gen = torch.Generator(device="cpu").manual_seed(77)
+    x0 = torch.randn((LATENTS * LENGTH, cfg.hidden), generator=gen).to(torch.bfloat16).to(dev)
+    x = torch.empty_like(x0)
+    for _ in range(args.warmup):
+        x.copy_(x0)
+        model.forward_(x, freqs)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("k2b_step")  # ncu --nvtx --nvtx-include k2b_step/
+    x.copy_(x0)
+    model.forward_(x, freqs)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print(json.dumps({"profile_passes": args.warmup + 1, "launches_per_pass": 1 + 7 * cfg.blocks}), flush=True)
+
+
 # --------------------------------------------------------------------- main
 
 def main():
@@ -299,9 +328,14 @@ def main():
                     help="profile mode: norm_quant|qkv|out_proj|gate_up|down|attention on one small case")
     ap.add_argument("--rows", type=int, default=LENGTH)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--profile", action="store_true",
+                    help="profile mode: only `warmup` + one forward pass of the config-4 job (ncu launch lists)")
     args = ap.parse_args()
     if args.kernel:
         run_kernel_case(args)
+        return
+    if args.profile:
+        run_profile_pass(args)
         return
     args.warmup = max(args.warmup, 3)
 

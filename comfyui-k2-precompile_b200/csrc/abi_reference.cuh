@@ -11,6 +11,24 @@
 //     k2_norm_mod_quant4 (the reference's two enums, native_runtime.cpp:83
 //     and kernels/joint_projection.cu:208); fp16 activations are rejected.
 // Return codes: 0, or cudaErrorInvalidValue for unsupported shapes/dtypes.
+// The reference's void exports (k2_norm, k2_quant4, k2_elementwise, k2_rope)
+// cannot return a status: they launch nothing on unsupported input and leave
+// the status for k2b_shim_status() (the reference's callers check
+// cudaGetLastError() after them, native_runtime.cpp:265,284).
+
+namespace {
+thread_local int g_shim_status = 0;
+void shim_status(int rc) {
+  if (rc) g_shim_status = rc;
+}
+}  // namespace
+
+// Last non-zero status of a void shim on this host thread (0 if none).
+K2B_EXPORT int k2b_shim_status(int reset) {
+  const int rc = g_shim_status;
+  if (reset) g_shim_status = 0;
+  return rc;
+}
 
 // kernels/norm_quant.cu:89-91
 K2B_EXPORT int k2_norm_mod_quant4(const void* x, const void* norm, const void* scale, const void* shift, void* q,
@@ -50,4 +68,45 @@ K2B_EXPORT int k2_int4_qk_norm_rope(void* a, void* w, void* xs, void* ws, void* 
   if (dtype != 0 || n % 256) return (int)cudaErrorInvalidValue;
   SegDesc d = {SEG_QKNORM, n, w, ws, output, n, static_cast<const float*>(norm), eps, nullptr, nullptr, nullptr};
   return gemm_launch(a, xs, m, k, &d, 1, m, static_cast<const float*>(freqs), nullptr, nullptr, (cudaStream_t)stream);
+}
+
+// kernels/native_dispatch.cu:79-83 (dtype 2 = bf16; scale == null: plain RMSNorm)
+K2B_EXPORT void k2_norm(const void* x, const void* w, const void* scale, const void* shift, void* y, int rows, int d,
+                        int length, int cut, int batch, float eps, int dtype, void* stream) {
+  shim_status(dtype != 2 ? (int)cudaErrorInvalidValue
+                         : k2b_norm_mod(x, w, scale, shift, y, rows, d, length, cut, batch, eps, stream));
+}
+
+// kernels/native_dispatch.cu:23-25 (group 128, dtype 2; scales fp16 [m, k/128])
+K2B_EXPORT void k2_quant4(const void* x, void* q, void* s, int64_t m, int64_t k, int group, int dtype, void* stream) {
+  shim_status(group != 128 || dtype != 2 || m > INT32_MAX || k > INT32_MAX
+                  ? (int)cudaErrorInvalidValue
+                  : k2b_rotate_quant(x, q, s, (int)m, (int)k, stream));
+}
+
+// kernels/native_dispatch.cu:84-89 (dtype 2)
+K2B_EXPORT void k2_elementwise(const void* a, const void* b, const void* r, void* y, int64_t n, int mode, int width,
+                               int dtype, void* stream) {
+  shim_status(dtype != 2 ? (int)cudaErrorInvalidValue : k2b_elementwise(a, b, r, y, (long long)n, mode, width, stream));
+}
+
+// kernels/native_dispatch.cu:90-95 (dtype 2)
+K2B_EXPORT void k2_rope(const void* q, const void* k, const void* f, void* qo, void* ko, int batch, int length, int qh,
+                        int kh, int dim, int fb, int dtype, void* stream) {
+  shim_status(dtype != 2 ? (int)cudaErrorInvalidValue
+                         : k2b_rope(q, k, f, qo, ko, batch, length, qh, kh, dim, fb, stream));
+}
+
+// kernels/joint_projection.cu:212-214: output = gated residual projection,
+// normalized = bf16 RMSNorm + modulation of it (batch 1, scale/shift [n]).
+// The reference's counters scratch (grid-wide row-sum hand-off) is not used:
+// the two stages run as two launches.
+K2B_EXPORT int k2_int4_residual_norm(void* a, void* w, void* xs, void* ws, void* gate, void* residual, void* norm,
+                                     void* scale, void* shift, void* output, void* normalized, void* counters, int m,
+                                     int n, int k, int dtype, float eps, void* stream) {
+  (void)counters;
+  if (dtype != 0) return (int)cudaErrorInvalidValue;
+  const int rc = k2b_gated_residual(a, xs, w, ws, gate, residual, output, m, m, n, k, stream);
+  if (rc) return rc;
+  return k2b_norm_mod(output, norm, scale, shift, normalized, m, n, m, -1, 1, eps, stream);
 }

@@ -1,0 +1,57 @@
+// elementwise.cuh -- the reference's small bf16 kernels that sit beside the
+// hot path: the activation / gated-residual elementwise op and the
+// standalone RoPE (kernels/native_dispatch.cu:63-77, k2_elementwise and
+// k2_rope).  HBM-bound and simple; they are here so the reference's
+// composed (non-fused) routes resolve to B200 code as well.
+#pragma once
+#include "k2b_common.cuh"
+
+namespace k2b {
+
+// mode 0: z = bf16(silu(a)), mode 1: z = bf16(sigmoid(a)); y = b ? bf16(z*b) : z.
+// mode 2: y = bf16(r + bf16(b * a[i % width]))  (gated residual, gate row a).
+__global__ void elementwise_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,
+                                   const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ y, int64_t n,
+                                   int mode, int width) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    if (mode == 2) {
+      const float z = bf16_round(__fmul_rn(__bfloat162float(b[i]), __bfloat162float(a[i % width])));
+      y[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(r[i]), z));
+      continue;
+    }
+    const float v = __bfloat162float(a[i]);
+    const float z = bf16_round(mode == 0 ? silu_contract(v) : sigmoid_contract(v));
+    y[i] = __float2bfloat16_rn(b ? __fmul_rn(z, __bfloat162float(b[i])) : z);
+  }
+}
+
+// Adjacent-pair RoPE on [batch, heads, length, dim] (contiguous) q and k:
+// o0 = bf16(fma(f0, a, f1*b)), o1 = bf16(fma(f2, a, f3*b)) with the 2x2
+// rotation of (token, pair) from f fp32 [fb, length, dim/2, 2, 2]
+// (fb = 1: shared by every batch row).
+__global__ void rope_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                            const float* __restrict__ f, __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko,
+                            int batch, int length, int qh, int kh, int dim, int fb) {
+  const int64_t rows = (int64_t)batch * length * (qh + kh);
+  const int half = dim / 2;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int h = (int)(row % (qh + kh));
+    const int token = (int)((row / (qh + kh)) % length);
+    const int bi = (int)(row / ((int64_t)(qh + kh) * length));
+    const bool isq = h < qh;
+    const __nv_bfloat16* src = isq ? q : k;
+    __nv_bfloat16* dst = isq ? qo : ko;
+    const int heads = isq ? qh : kh, head = isq ? h : h - qh;
+    const int64_t base = (((int64_t)bi * heads + head) * length + token) * dim;
+    const float* rot0 = f + ((int64_t)(fb == 1 ? 0 : bi) * length + token) * half * 4;
+    for (int p = threadIdx.x; p < half; p += blockDim.x) {
+      const float a = __bfloat162float(src[base + 2 * p]), v = __bfloat162float(src[base + 2 * p + 1]);
+      const float4 rot = *reinterpret_cast<const float4*>(rot0 + 4 * p);
+      dst[base + 2 * p] = __float2bfloat16_rn(__fmaf_rn(rot.x, a, __fmul_rn(rot.y, v)));
+      dst[base + 2 * p + 1] = __float2bfloat16_rn(__fmaf_rn(rot.z, a, __fmul_rn(rot.w, v)));
+    }
+  }
+}
+
+}  // namespace k2b

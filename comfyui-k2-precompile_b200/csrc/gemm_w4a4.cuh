@@ -56,6 +56,7 @@ constexpr int GEMM_BN = 256;
 constexpr int GEMM_STAGES = 4;   // prepared W half + unpacked A
 constexpr int GEMM_PSTAGES = 4;  // packed A and W scales
 constexpr int GEMM_EPI_WARPS = 16;
+constexpr int kGemmBand = 16;    // M pairs (of 256 rows) per band of the tile order
 constexpr int GEMM_THREADS = 128 + 32 * GEMM_EPI_WARPS;  // 640
 // Registers per thread the kernel is compiled with (65536 / 640 rounded down
 // to the allocation granule).  Warpgroup 0 drops to 32 and the epilogue
@@ -180,9 +181,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();  // 0: leader (issues the pair's MMAs), 1: peer
   const bool leader = rank == 0;
-  const int m0 = blockIdx.x * GEMM_BM;
+  // Banded tile order: the launch-order index of the CTA pair is remapped so
+  // that kGemmBand consecutive M pairs (4096 rows of packed A, ~13 MB) walk
+  // every N tile before the next band starts.  A band stays in L2 while the
+  // weights stream once per band (launch order alone re-streams all of A for
+  // each N tile).  Both CTAs of a pair decode the same (pair, N tile).
+  const int pairs_m = (int)(gridDim.x >> 1), ntiles = (int)gridDim.y;
+  const int lin = (int)blockIdx.y * pairs_m + (int)(blockIdx.x >> 1);
+  const int band0 = lin / (kGemmBand * ntiles) * kGemmBand;
+  const int band_pairs = min(kGemmBand, pairs_m - band0);
+  const int in_band = lin - band0 * ntiles;
+  const int ntile = in_band / band_pairs;
+  const int m0 = (2 * (band0 + in_band % band_pairs) + (int)rank) * GEMM_BM;
   // Segment of this N tile.
-  int seg = 0, tile = blockIdx.y;
+  int seg = 0, tile = ntile;
   while (seg + 1 < p.nseg && tile >= p.seg[seg].tiles) {
     tile -= p.seg[seg].tiles;
     ++seg;

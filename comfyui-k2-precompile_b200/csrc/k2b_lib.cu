@@ -13,6 +13,7 @@
 #include "attention.cuh"
 #include "gemm_w4a4.cuh"
 #include "k2b_common.cuh"
+#include "elementwise.cuh"
 #include "norm_quant.cuh"
 
 #define K2B_EXPORT extern "C" __attribute__((visibility("default")))
@@ -73,25 +74,26 @@ static int make_map_4d_bf16(CUtensorMap* map, const void* base, uint64_t D, uint
 static int launch_status() { return (int)cudaGetLastError(); }
 
 // ----------------------------------------------------------- norm_quant
-template <bool NORM>
+template <bool NORM, bool MOD, bool QUANT>
 static int norm_quant_launch(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                              int rows, int K, int length, int cut, int batch, float eps, cudaStream_t st) {
-  if (rows <= 0 || K <= 0 || K % 512 || K > 16384 || (NORM && (length <= 0 || batch <= 0)))
+  if (rows <= 0 || K <= 0 || K % 512 || K > 16384 || (MOD && (length <= 0 || batch <= 0)))
     return (int)cudaErrorInvalidValue;
-  if (!aligned16(x) || !aligned16(q) || !s || (NORM && (!aligned16(w) || !aligned16(scale) || !aligned16(shift))))
+  if (!aligned16(x) || !aligned16(q) || (QUANT && !s) || (NORM && !aligned16(w)) ||
+      (MOD && (!aligned16(scale) || !aligned16(shift))))
     return (int)cudaErrorInvalidValue;
-  // One wave of resident CTAs looping over 16-row tiles; the residency is
+  // One wave of resident CTAs looping over row tiles; the residency is
   // queried once per device (the same value may be stored twice by racing
   // first calls, which is harmless).
-  static int resident[2][64];
+  static int resident[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
   if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-  int& per_sm = resident[NORM ? 1 : 0][dev];
+  int& per_sm = resident[dev];
   if (per_sm == 0) {
     int n = 0, sms = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, norm_quant_kernel<NORM>, kNqThreads, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, norm_quant_kernel<NORM, MOD, QUANT>, kNqThreads, 0);
     if (e != cudaSuccess) return (int)e;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return (int)e;
@@ -99,7 +101,7 @@ static int norm_quant_launch(const void* x, const void* w, const void* scale, co
   }
   const int tiles = (rows + kNqRows - 1) / kNqRows;
   const int grid = tiles < per_sm ? tiles : per_sm;
-  norm_quant_kernel<NORM><<<grid, kNqThreads, 0, st>>>(
+  norm_quant_kernel<NORM, MOD, QUANT><<<grid, kNqThreads, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(w), static_cast<const __nv_bfloat16*>(scale),
       static_cast<const __nv_bfloat16*>(shift), static_cast<uint8_t*>(q), static_cast<__half*>(s), rows, K, length,
       cut, batch, eps);
@@ -309,11 +311,49 @@ K2B_EXPORT int k2b_device_error(int reset, void* stream) {
 
 K2B_EXPORT int k2b_norm_quant(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                               int rows, int K, int length, int cut, int batch, float eps, void* stream) {
-  return norm_quant_launch<true>(x, w, scale, shift, q, s, rows, K, length, cut, batch, eps, (cudaStream_t)stream);
+  return norm_quant_launch<true, true, true>(x, w, scale, shift, q, s, rows, K, length, cut, batch, eps,
+                                             (cudaStream_t)stream);
 }
 
 K2B_EXPORT int k2b_rotate_quant(const void* x, void* q, void* s, int rows, int K, void* stream) {
-  return norm_quant_launch<false>(x, nullptr, nullptr, nullptr, q, s, rows, K, 1, -1, 1, 0.0f, (cudaStream_t)stream);
+  return norm_quant_launch<false, false, true>(x, nullptr, nullptr, nullptr, q, s, rows, K, 1, -1, 1, 0.0f,
+                                               (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_norm_mod(const void* x, const void* w, const void* scale, const void* shift, void* y, int rows,
+                            int K, int length, int cut, int batch, float eps, void* stream) {
+  if ((scale == nullptr) != (shift == nullptr)) return (int)cudaErrorInvalidValue;
+  if (scale)
+    return norm_quant_launch<true, true, false>(x, w, scale, shift, y, nullptr, rows, K, length, cut, batch, eps,
+                                                (cudaStream_t)stream);
+  return norm_quant_launch<true, false, false>(x, w, nullptr, nullptr, y, nullptr, rows, K, 1, -1, 1, eps,
+                                               (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_elementwise(const void* a, const void* b, const void* r, void* y, long long n, int mode, int width,
+                               void* stream) {
+  if (n < 0 || !a || !y || mode < 0 || mode > 2 || (mode == 2 && (!b || !r || width <= 0)))
+    return (int)cudaErrorInvalidValue;
+  if (n == 0) return 0;
+  const long long blocks = (n + 255) / 256;
+  const int grid = (int)(blocks < 148 * 32 ? blocks : 148 * 32);
+  elementwise_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), static_cast<const __nv_bfloat16*>(r),
+      static_cast<__nv_bfloat16*>(y), (int64_t)n, mode, width);
+  return launch_status();
+}
+
+K2B_EXPORT int k2b_rope(const void* q, const void* k, const void* f, void* qo, void* ko, int batch, int length, int qh,
+                        int kh, int dim, int fb, void* stream) {
+  if (batch <= 0 || length <= 0 || qh < 0 || kh < 0 || qh + kh == 0 || dim <= 0 || dim % 2 || (fb != 1 && fb != batch))
+    return (int)cudaErrorInvalidValue;
+  if (!f || !aligned16(f) || (qh && (!q || !qo)) || (kh && (!k || !ko))) return (int)cudaErrorInvalidValue;
+  const long long rows = (long long)batch * length * (qh + kh);
+  const int grid = (int)(rows < 148 * 64 ? rows : 148 * 64);
+  rope_kernel<<<grid, 64, 0, (cudaStream_t)stream>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), static_cast<const float*>(f),
+      static_cast<__nv_bfloat16*>(qo), static_cast<__nv_bfloat16*>(ko), batch, length, qh, kh, dim, fb);
+  return launch_status();
 }
 
 K2B_EXPORT int k2b_prepare_weight(const void* w_packed, const void* w_scale, void* w_prepared, void* scale_t, int n,

@@ -62,7 +62,10 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 constexpr int kNqGroupFloats = 144;
 __device__ __forceinline__ constexpr int nq_pad_chunk(int c) { return c + (c >> 3); }
 
-template <bool NORM>
+// NORM: RMS-normalise (y = bf16(x*inv*(w+1))); MOD: then apply the adaLN
+// scale/shift; QUANT: then rotate + INT4 (else store the bf16 row to q).
+//   <1,1,1> norm_quant   <0,0,1> rotate_quant   <1,1,0> norm_mod   <1,0,0> norm
+template <bool NORM, bool MOD, bool QUANT>
 __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bfloat16* __restrict__ x,
                                                                 const float* __restrict__ w,
                                                                 const __nv_bfloat16* __restrict__ scale,
@@ -134,10 +137,12 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
         const float total = __fadd_rn(__fadd_rn(w2, w0), __fadd_rn(w3, w1));
         if (lane == 0) {
           s_inv[r] = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), eps));
-          const int row = row0 + r;
-          int bb = row / length;
-          if (cut >= 0 && row % length >= cut) bb += batch;
-          s_lat[r] = bb;
+          if constexpr (MOD) {
+            const int row = row0 + r;
+            int bb = row / length;
+            if (cut >= 0 && row % length >= cut) bb += batch;
+            s_lat[r] = bb;
+          }
         }
       }
       __syncthreads();
@@ -149,7 +154,7 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
       float2 w1[8];
       uint32_t fm[8], sh[8];
       int bcur = -1;
-      if constexpr (NORM) {
+      if constexpr (NORM) {  // (w + 1) of this lane's 16 columns
         const float4* wp = reinterpret_cast<const float4*>(w + col);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -163,7 +168,7 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
       // one row: x words (xa, xb) -> codes at qp, scale at sp
       auto row_body = [&](const uint4 xa, const uint4 xb, int r, uint8_t* qp, __half* sp) {
         uint32_t vw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-        if constexpr (NORM) {
+        if constexpr (MOD) {
           const int bb = s_lat[r];
           if (bb != bcur) {  // warp-uniform: every lane works on the same row
             bcur = bb;
@@ -179,6 +184,8 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
               sh[k] = hv[k];
             }
           }
+        }
+        if constexpr (NORM) {
           const float inv = s_inv[r];
           const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
@@ -189,9 +196,19 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
             // 2*8+2 bits), which is the reference's fp32-then-bf16 rounding.  The
             // .rn forms keep the compiler from contracting them into one fma.
             const float2 t = __fmul2_rn(__fmul2_rn(bf2_unpack(vw[k]), inv2), w1[k]);
-            const __nv_bfloat162 y = __hmul2_rn(__float22bfloat162_rn(t), bf2_from(fm[k]));
-            vw[k] = bf2_bits(__hadd2_rn(y, bf2_from(sh[k])));
+            if constexpr (MOD) {
+              const __nv_bfloat162 y = __hmul2_rn(__float22bfloat162_rn(t), bf2_from(fm[k]));
+              vw[k] = bf2_bits(__hadd2_rn(y, bf2_from(sh[k])));
+            } else {
+              vw[k] = bf2_bits(__float22bfloat162_rn(t));
+            }
           }
+        }
+        if constexpr (!QUANT) {  // bf16 row out (q holds the bf16 output)
+          uint4* yo = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(q) + (int64_t)(row0 + r) * K + col);
+          yo[0] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+          yo[1] = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+          return;
         }
         // layout A: p[k] = (x[2k], x[2k+1]) of this lane's 16 columns
         float2 p[8];

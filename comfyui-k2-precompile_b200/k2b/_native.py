@@ -41,6 +41,15 @@ SIGNATURES = {
     "k2_int4_swiglu": (_I, [_P] * 7 + [_I] * 4 + [_P]),
     "k2_int4_gated_residual": (_I, [_P] * 7 + [_I] * 5 + [_P]),
     "k2_int4_qk_norm_rope": (_I, [_P] * 7 + [_I] * 4 + [_F, _P]),
+    "k2b_norm_mod": (_I, [_P] * 5 + [_I] * 5 + [_F, _P]),
+    "k2b_elementwise": (_I, [_P] * 4 + [_LL, _I, _I, _P]),
+    "k2b_rope": (_I, [_P] * 5 + [_I] * 6 + [_P]),
+    "k2_int4_residual_norm": (_I, [_P] * 12 + [_I] * 4 + [_F, _P]),
+    "k2_norm": (None, [_P] * 5 + [_I] * 5 + [_F, _I, _P]),
+    "k2_quant4": (None, [_P] * 3 + [ctypes.c_int64] * 2 + [_I, _I, _P]),
+    "k2_elementwise": (None, [_P] * 4 + [ctypes.c_int64, _I, _I, _I, _P]),
+    "k2_rope": (None, [_P] * 5 + [_I] * 7 + [_P]),
+    "k2b_shim_status": (_I, [_I]),
 }
 
 _lib = None

@@ -108,6 +108,60 @@ def norm_quant(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: tor
     return q, s
 
 
+def norm_mod(x: torch.Tensor, w: torch.Tensor, scale: Optional[torch.Tensor] = None,
+             shift: Optional[torch.Tensor] = None, *, length: Optional[int] = None, cut: int = -1,
+             eps: float = 1e-6) -> torch.Tensor:
+    """bf16 RMSNorm (+ adaLN when scale/shift are given), the rounding points
+    of norm_quant without the quantisation (k2_native::norm_mod, k2_norm).
+    Returns bf16 shaped like x."""
+    _cuda(x, w, scale, shift)
+    _need((scale is None) == (shift is None), "norm_mod: scale and shift go together")
+    _need(x.dtype == torch.bfloat16 and w.dtype == torch.float32, "norm_mod: bf16 x, fp32 w expected")
+    K = int(x.shape[-1])
+    rows = x.numel() // K
+    _need(w.numel() == K, "norm_mod: width mismatch")
+    if length is None:
+        length = int(x.shape[-2]) if x.dim() == 3 else rows
+    batch = max(1, rows // length)
+    if scale is not None:
+        _need(scale.dtype == torch.bfloat16 and shift.dtype == torch.bfloat16 and scale.shape[-1] == K and
+              shift.numel() == scale.numel(), "norm_mod: bf16 modulation [nb, K] expected")
+        _need(scale.numel() // K >= (2 * batch if cut >= 0 else batch), "norm_mod: modulation rows do not cover the batch")
+    y = torch.empty_like(x)
+    check(lib().k2b_norm_mod(_p(x), _p(w), _p(scale), _p(shift), _p(y), rows, K, length, cut, batch,
+                             ctypes.c_float(eps), _stream()), "k2b_norm_mod")
+    return y
+
+
+def elementwise(a: torch.Tensor, b: Optional[torch.Tensor], r: Optional[torch.Tensor], mode: int,
+                width: int = 0) -> torch.Tensor:
+    """k2_elementwise (kernels/native_dispatch.cu:63-70): mode 0 silu(a)[*b],
+    1 sigmoid(a)[*b], 2 r + b*a[i % width] (bf16, each step rounded)."""
+    _cuda(a, b, r)
+    for t in (a, b, r):
+        _need(t is None or t.dtype == torch.bfloat16, "elementwise: bf16 expected")
+    out_like = r if mode == 2 else a
+    _need(out_like is not None, "elementwise: mode 2 needs a residual")
+    y = torch.empty_like(out_like)
+    check(lib().k2b_elementwise(_p(a), _p(b), _p(r), _p(y), y.numel(), mode, width, _stream()), "k2b_elementwise")
+    return y
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, freqs: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """k2_native::rope (native_runtime.cpp:312-317): q [B,Hq,L,D], k [B,Hk,L,D]
+    bf16, freqs fp32 [fb, ..., L, D/2, 2, 2] with fb = 1 or B."""
+    _cuda(q, k, freqs)
+    _need(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and freqs.dtype == torch.float32, "rope: dtypes")
+    B, Hq, L, D = q.shape
+    _need(k.shape[0] == B and k.shape[2] == L and k.shape[3] == D, "rope: q/k shapes")
+    per = L * (D // 2) * 4
+    _need(freqs.numel() % per == 0 and freqs.numel() // per in (1, B), "rope: freqs shape")
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    check(lib().k2b_rope(_p(q), _p(k), _p(freqs), _p(qo), _p(ko), B, L, Hq, int(k.shape[1]), D,
+                         freqs.numel() // per, _stream()), "k2b_rope")
+    return qo, ko
+
+
 def rotate_quant(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """bf16 [..., K] -> (uint8 [rows, K/2], fp16 [rows, K/128])."""
     _cuda(x)
@@ -262,6 +316,7 @@ def device_error(reset: bool = True) -> int:
 
 
 __all__ = [
-    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "rotate_quant", "gemm_f32", "gemm_bf16", "qkv",
+    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_mod", "elementwise", "rope", "rotate_quant",
+    "gemm_f32", "gemm_bf16", "qkv",
     "gated_residual", "swiglu_quant", "swiglu_bf16", "attention", "attention_quant", "device_error",
 ]

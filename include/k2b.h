@@ -28,6 +28,8 @@
 #ifndef K2B_H
 #define K2B_H
 
+#include <stdint.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -49,7 +51,7 @@ int k2b_device_error(int reset, void* stream);
  * the modulation row is b = row/length (+batch when cut >= 0 and
  * row%length >= cut), kernels/norm_quant.cu:32.
  * x bf16 [rows,K]; w fp32 [K]; scale/shift bf16 [nb,K]; q u8 [rows,K/2];
- * s fp16 [rows,K/128].  K must be one of 512*{1,2,4,8,12,16,24,32}. */
+ * s fp16 [rows,K/128].  K a multiple of 512, at most 16384. */
 int k2b_norm_quant(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                    int rows, int K, int length, int cut, int batch, float eps, void* stream);
 
@@ -58,6 +60,26 @@ int k2b_norm_quant(const void* x, const void* w, const void* scale, const void* 
  * comfy-kitchen quantize_int4_rowwise_convrot64 via k2_quant4,
  * kernels/native_dispatch.cu:23-25).  Same K constraint as k2b_norm_quant. */
 int k2b_rotate_quant(const void* x, void* q, void* s, int rows, int K, void* stream);
+
+/* bf16 RMSNorm (+ adaLN modulation when scale/shift are given) with the
+ * rounding points and reduction order of k2b_norm_quant, output bf16
+ * [rows,K].  Replaces k2_norm / norm_mod (kernels/native_dispatch.cu:44-62,
+ * 79-83) behind k2_native::norm_mod and residual_norm (native_runtime.cpp:
+ * 262-266, 513).  scale and shift are both given or both null. */
+int k2b_norm_mod(const void* x, const void* w, const void* scale, const void* shift, void* y, int rows, int K,
+                 int length, int cut, int batch, float eps, void* stream);
+
+/* bf16 elementwise of kernels/native_dispatch.cu:63-70 / k2_elementwise:
+ * mode 0 y = bf16(silu(a)) [* b], mode 1 y = bf16(sigmoid(a)) [* b]
+ * (b may be null), mode 2 y = bf16(r + bf16(b * a[i % width])). */
+int k2b_elementwise(const void* a, const void* b, const void* r, void* y, long long n, int mode, int width,
+                    void* stream);
+
+/* Adjacent-pair RoPE of kernels/native_dispatch.cu:71-77 / k2_rope on bf16
+ * [batch, heads, length, dim] q and k; f fp32 [fb, length, dim/2, 2, 2],
+ * fb = 1 or batch. */
+int k2b_rope(const void* q, const void* k, const void* f, void* qo, void* ko, int batch, int length, int qh, int kh,
+             int dim, int fb, void* stream);
 
 /* ---------------------------------------------------- weight preparation --
  * Registration-time conversion of a packed INT4 weight [n, k/2] + fp16 group
@@ -183,6 +205,24 @@ int k2_int4_gated_residual(void* a, void* w, void* xs, void* ws, void* gate, voi
                            int n, int k, int dtype, int config, void* stream); /* kernels/int4_epilogue.cu:77-78 */
 int k2_int4_qk_norm_rope(void* a, void* w, void* xs, void* ws, void* norm, void* freqs, void* output, int m, int n,
                          int k, int dtype, float eps, void* stream); /* kernels/qk_norm_rope.cu:135 */
+
+int k2_int4_residual_norm(void* a, void* w, void* xs, void* ws, void* gate, void* residual, void* norm, void* scale,
+                          void* shift, void* output, void* normalized, void* counters, int m, int n, int k, int dtype,
+                          float eps, void* stream); /* kernels/joint_projection.cu:212-214 */
+/* The reference's void exports (kernels/native_dispatch.cu:23-29, 79-95):
+ * unsupported input launches nothing and sets the status k2b_shim_status()
+ * returns (bf16 = dtype 2 only; k2_quant4: group 128, fp16 group scales). */
+void k2_norm(const void* x, const void* w, const void* scale, const void* shift, void* y, int rows, int d, int length,
+             int cut, int batch, float eps, int dtype, void* stream);
+void k2_quant4(const void* x, void* q, void* s, int64_t m, int64_t k, int group, int dtype, void* stream);
+void k2_elementwise(const void* a, const void* b, const void* r, void* y, int64_t n, int mode, int width, int dtype,
+                    void* stream);
+void k2_rope(const void* q, const void* k, const void* f, void* qo, void* ko, int batch, int length, int qh, int kh,
+             int dim, int fb, int dtype, void* stream);
+/* Last non-zero status of a void shim on this host thread; reset clears it.
+ * No counterpart in the reference (its void exports rely on
+ * cudaGetLastError()). */
+int k2b_shim_status(int reset);
 
 #ifdef __cplusplus
 }
