@@ -3,12 +3,16 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: 8 independent latents x 4224 tokens
+Workload (config 4 of the benchmark): 8 independent latents x 4224 tokens
 (128 text + 64x64 image), 28 Krea2-shaped W4A4 blocks (hidden 6144, 48/12
 heads, MLP 16384), random-init weights (N(0,0.02), H128-rotated, INT4),
 synthetic N(0,1) hidden states.  One step = the 28-block forward of all 8
 latents; with N ranks each rank runs 8/N latents (batch sharding, no
-collective: "scaling": "strong" over the fixed 8-latent job).  The metric's
+collective: "scaling": "strong" over the fixed 8-latent job).  ``--tp T``
+runs T-way KV-head tensor parallelism inside groups of T ranks (NCCL
+reduce-scatter after the out- and down-projections, INT4 all-gather before
+the QKV and gate/up projections, k2b.parallel) and batch sharding across the
+N/T groups.  The metric's
 other half, the 28-block forward at 4050 tokens batch 1 (config 3), is
 measured on rank 0 at N=1 and reported as "forward_ms_4050".
 
@@ -317,12 +321,90 @@ def run_profile_pass(args):
 
 # --------------------------------------------------------------------- main
 
+class Workload:
+    """One rank's share of the config-4 job and how one step runs it.
+
+    tp == 1: the native block loop (k2b_forward_blocks) over this rank's
+    latents, 8 events per block (7 kernels).  tp > 1: k2b.parallel.TPBlocks
+    over this rank's rows of its group's latents, 13 events per block
+    (12 phases: 9 kernels and 4 NCCL collectives)."""
+
+    def __init__(self, torch, cfg, topo, dev, latents):
+        from k2b.model import Krea2Blocks, rope_positions, rope_table, synthetic_blocks
+        from k2b.parallel import PHASES, TPBlocks, TPPlan, shard_fn
+
+        self.torch, self.cfg, self.topo, self.latents = torch, cfg, topo, latents
+        self.freqs = rope_table(rope_positions(TEXT, GRID, GRID), (64, 64), cfg.theta).to(dev)
+        rows = latents * LENGTH
+        if topo.tp == 1:
+            self.blocks = synthetic_blocks(cfg, latents, seed=1234, device=dev)
+            self.model = Krea2Blocks(cfg, self.blocks, latents, LENGTH, device=dev)
+            self.rows_here = rows
+            self.phases = OP_NAMES
+            self.ev_per_block = 8
+        else:
+            plan = TPPlan.of(cfg, topo.tp, topo.tp_rank)
+            self.blocks = synthetic_blocks(cfg, latents, seed=1234, device=dev, shard=shard_fn(plan))
+            self.model = TPBlocks(cfg, self.blocks, plan, topo.tp_group, latents, LENGTH, device=dev)
+            self.rows_here = self.model.shard.chunk
+            self.phases = PHASES
+            self.ev_per_block = len(PHASES)
+        self.plan_rows = rows
+
+    def events(self):
+        n = self.ev_per_block * self.cfg.blocks + (0 if self.topo.tp == 1 else 1)
+        return [self.torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+    def step(self, x, events=None):
+        self.model.forward_(x, self.freqs, events=events)
+
+    def phase_times(self, ev):
+        """[(phase, ms)] for every block from one step's events."""
+        out = []
+        nb, e = self.cfg.blocks, self.ev_per_block
+        for b in range(nb):
+            for i, n in enumerate(self.phases):
+                out.append((n, ev[e * b + i].elapsed_time(ev[e * b + i + 1])))
+        return out
+
+    def phase_work(self):
+        """Algorithmic work per launch of each phase: (amount, unit kind)."""
+        cfg, t = self.cfg, self.topo.tp
+        H, F, L = cfg.hidden, cfg.mlp, LENGTH
+        rows = self.plan_rows
+        hq, kv, f = cfg.heads // t, cfg.kvheads // t, F // t
+        own = rows if t == 1 else self.model.shard.count
+        nq = own * (H * 2 + H // 2 + (H // 128) * 2) + H * 4 + 2 * self.latents * H * 2
+        w = {"qkv": (2 * rows * (hq + 2 * kv) * 128 * H, "int"), "attn": (4 * self.latents * hq * L * L * 128, "bf16"),
+             "out": (2 * rows * H * hq * 128, "int"), "gu": (2 * rows * 2 * f * H, "int"),
+             "down": (2 * rows * H * f, "int"), "nq": (nq, "bytes")}
+        if t == 1:
+            return {"norm_quant_pre": w["nq"], "qkv_qknorm_rope": w["qkv"], "attention_quant": w["attn"],
+                    "out_proj_residual": w["out"], "norm_quant_post": w["nq"], "gate_up_swiglu_quant": w["gu"],
+                    "down_proj_residual": w["down"]}
+        c = self.model.shard.chunk
+        gather = (t - 1) * c * (H // 2 + (H // 128) * 2)  # bytes each rank receives
+        rs = (t - 1) * c * H * 4                            # bytes each rank receives (fp32)
+        add = own * (H * 4 + 2 * H * 2)
+        return {"norm_quant_pre": w["nq"], "gather_act": (gather, "link"), "qkv_qknorm_rope": w["qkv"],
+                "attention_quant": w["attn"], "out_proj_partial": w["out"], "reduce_scatter_out": (rs, "link"),
+                "gated_add_norm_quant_post": (w["nq"][0] + add, "bytes"), "gather_mlp_in": (gather, "link"),
+                "gate_up_swiglu_quant": w["gu"], "down_proj_partial": w["down"],
+                "reduce_scatter_down": (rs, "link"), "gated_add": (add, "bytes")}
+
+    def launches_per_step(self):
+        return self.cfg.blocks * (7 if self.topo.tp == 1 else 9)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tp", type=int, default=1,
+                    help="KV-head tensor-parallel degree (1, 2, 4); the remaining factor of the world is batch "
+                         "sharding (8 GPUs: --tp 4 gives 4-way head TP x 2-way batch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="profile mode: norm_quant|qkv|out_proj|gate_up|down|attention on one small case")
@@ -358,21 +440,31 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     from k2b import ops
-    from k2b.model import Krea2Blocks, ModelConfig, block_flops, rope_positions, rope_table, synthetic_blocks
+    from k2b.model import Krea2Blocks, ModelConfig
+    from k2b.parallel import topology
 
-    if LATENTS % world:
-        raise SystemExit("the 8-latent job splits across 1, 2, 4 or 8 ranks")
-    local = LATENTS // world
+    tp = args.tp if world > 1 else 1
+    topo = topology(world, rank, tp)
+    lat0, lat1 = topo.latent_range(LATENTS)
+    local = lat1 - lat0
     cfg = ModelConfig()
     peaks, peak_kind = measured_peaks()
     int8_tops = int8_peak_tops(torch) if rank == 0 else None
 
-    blocks = synthetic_blocks(cfg, local, seed=1234, device=dev)
-    freqs = rope_table(rope_positions(TEXT, GRID, GRID), (64, 64), cfg.theta).to(dev)
-    model = Krea2Blocks(cfg, blocks, local, LENGTH, device=dev)
-    rows = local * LENGTH
-    gen = torch.Generator(device="cpu").manual_seed(77 + rank)
-    x_host = torch.randn((rows, cfg.hidden), generator=gen).to(torch.bfloat16).pin_memory()
+    wl = Workload(torch, cfg, topo, dev, local)
+    freqs = wl.freqs
+    rows = wl.rows_here
+    # this rank's hidden-state rows of its group's latents (whole latents when tp == 1)
+    gen = torch.Generator(device="cpu").manual_seed(77 + topo.dp_index)
+    x_group = torch.randn((local * LENGTH, cfg.hidden), generator=gen).to(torch.bfloat16)
+    if tp == 1:
+        x_host = x_group.pin_memory()
+    else:
+        sh = wl.model.shard
+        x_host = torch.zeros((sh.chunk, cfg.hidden), dtype=torch.bfloat16)
+        x_host[:sh.count] = x_group[sh.base:sh.base + sh.count]
+        x_host = x_host.pin_memory()
+    del x_group
     x0 = x_host.to(dev)
     x = torch.empty_like(x0)
     out_host = torch.empty_like(x_host).pin_memory()
@@ -389,15 +481,14 @@ def main():
         return float(t.item())
 
     # ---------------------------------------------------- device-resident timing
-    nb = cfg.blocks
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(8 * nb)] for _ in range(args.steps)]
+    events = [wl.events() for _ in range(args.steps)]
     for ev in events:  # create the CUDA events before their handles are passed down
         for e in ev:
             e.record()
     torch.cuda.synchronize()
     for _ in range(args.warmup):
         x.copy_(x0)
-        model.forward_(x, freqs)
+        wl.step(x)
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -409,7 +500,7 @@ def main():
     start.record()
     for i in range(args.steps):
         x.copy_(x0)
-        model.forward_(x, freqs, events=events[i])
+        wl.step(x, events=events[i])
     end.record()
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
@@ -421,45 +512,46 @@ def main():
     ms_per_step = elapsed_ms / args.steps
     value = LATENTS / (ms_per_step / 1e3)
 
-    # per-kernel durations inside the timed region
-    per_op = {n: [] for n in OP_NAMES}
+    # per-phase durations inside the timed region
+    per_op = {n: [] for n in wl.phases}
     for ev in events:
-        for b in range(nb):
-            for i, n in enumerate(OP_NAMES):
-                per_op[n].append(ev[8 * b + i].elapsed_time(ev[8 * b + i + 1]))
+        for n, ms in wl.phase_times(ev):
+            per_op[n].append(ms)
     total_ms = sum(sum(v) for v in per_op.values())
-    fl = block_flops(cfg, rows, LENGTH, local)
-    work = {"norm_quant_pre": None, "qkv_qknorm_rope": fl["qkv"], "attention_quant": fl["attn"],
-            "out_proj_residual": fl["out"], "norm_quant_post": None, "gate_up_swiglu_quant": fl["gate_up"],
-            "down_proj_residual": fl["down"]}
-    nq_bytes = rows * cfg.hidden * 2 + cfg.hidden * 4 + 2 * local * cfg.hidden * 2 + rows * cfg.hidden // 2 + \
-        rows * (cfg.hidden // 128) * 2
+    work = wl.phase_work()
     kernels = {}
     for n, ts in per_op.items():
+        if not ts:
+            continue
         avg = statistics.mean(ts)
+        amount, kind = work[n]
         d = {"launches": len(ts), "avg_us": avg * 1e3, "share": sum(ts) / total_ms}
-        if n.startswith("norm_quant"):
-            d["achieved"] = nq_bytes / (avg * 1e-3) / 1e9
+        if kind == "bytes":
+            d["achieved"] = amount / (avg * 1e-3) / 1e9
             d["unit"] = "GB/s"
             d["frac"] = d["achieved"] / peaks["hbm_gbs"]
-        elif n == "attention_quant":
-            d["achieved"] = work[n] / (avg * 1e-3) / 1e12
+        elif kind == "link":
+            d["achieved"] = amount / (avg * 1e-3) / 1e9
+            d["unit"] = "GB/s received per rank (NCCL)"
+            d["frac_of_peer_copy_770"] = d["achieved"] / 770.0
+        elif kind == "bf16":
+            d["achieved"] = amount / (avg * 1e-3) / 1e12
             d["unit"] = "TFLOP/s"
             d["frac"] = d["achieved"] / peaks["bf16_tflops_sustained"]
         else:
-            d["achieved"] = work[n] / (avg * 1e-3) / 1e12
+            d["achieved"] = amount / (avg * 1e-3) / 1e12
             d["unit"] = "TOP/s int"
             if int8_tops:
                 d["frac_of_int8_measured"] = d["achieved"] / int8_tops
             d["frac_of_int8_datasheet"] = d["achieved"] / 4500.0
         kernels[n] = d
-    dom = max(kernels, key=lambda k: kernels[k]["share"])
-    traffic = load_traffic().get(dom)
+    dom = max((k for k in kernels if work[k][1] == "int"), key=lambda k: kernels[k]["share"])
+    traffic = load_traffic().get(dom) if tp == 1 else None
 
     # ------------------------------------------------------------ end to end
     for _ in range(args.warmup):
         x.copy_(x_host, non_blocking=True)
-        model.forward_(x, freqs)
+        wl.step(x)
         out_host.copy_(x, non_blocking=True)
     torch.cuda.synchronize()
     barrier()
@@ -468,7 +560,7 @@ def main():
     s2.record()
     for _ in range(args.steps):
         x.copy_(x_host, non_blocking=True)
-        model.forward_(x, freqs)
+        wl.step(x)
         out_host.copy_(x, non_blocking=True)
     e2.record()
     torch.cuda.synchronize()
@@ -480,11 +572,13 @@ def main():
     # ------------------------------------------- config 3 (4050 tok, batch 1)
     fwd4050 = None
     if world == 1:
+        from k2b.model import rope_positions, rope_table
+
         L3 = 4050
         import copy
 
         b3 = []
-        for b in blocks:
+        for b in wl.blocks:
             c = copy.copy(b)
             c.mod = b.mod[:, :1].contiguous()
             b3.append(c)
@@ -520,7 +614,8 @@ def main():
                 "frac": kd.get("frac_of_int8_measured"),
                 "frac_of_datasheet_4500": kd.get("frac_of_int8_datasheet"),
                 "traffic": traffic,
-                "work_per_launch": work[dom], "avg_launch_us": kd["avg_us"]}
+                "work_per_launch": work[dom][0], "avg_launch_us": kd["avg_us"]}
+        par = f"batch-shard x{world}" if tp == 1 else f"kv-head TP x{tp} (row-sharded residual) x batch-shard x{topo.dp}"
         line = {
             "metric": METRIC, "value": value, "unit": "latents/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -528,7 +623,7 @@ def main():
             "config": {"workload": "config 4: 8 latents x 4224 tokens (128 text + 64x64 image), 28 Krea2 blocks",
                        "latents": LATENTS, "tokens_per_latent": LENGTH, "blocks": cfg.blocks,
                        "hidden": cfg.hidden, "heads": cfg.heads, "kvheads": cfg.kvheads, "mlp": cfg.mlp,
-                       "parallelism": f"batch-shard x{world}", "latents_per_gpu": local,
+                       "parallelism": par, "tp": tp, "dp": topo.dp, "latents_per_group": local,
                        "l2": "inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"},
             "forward_ms_4050": fwd4050,
             "e2e": {"value": e2e_value, "unit": "latents/s", "ms_per_step": e2e_ms,
@@ -539,13 +634,14 @@ def main():
             "peaks": {"hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops": peaks.get("bf16_tflops"),
                       "bf16_tflops_sustained": peaks.get("bf16_tflops_sustained"), "source": peak_kind,
                       "int8_tops": int8_tops},
-            "gpu_launches": 7 * cfg.blocks * args.steps,
+            "gpu_launches": wl.launches_per_step() * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "output_finite": finite,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        del wl
         dist.destroy_process_group()
 
 

@@ -65,7 +65,7 @@ K2B_EXPORT int k2_int4_gated_residual(void* a, void* w, void* xs, void* ws, void
 // kernels/qk_norm_rope.cu:135 (batch 1: freqs [m, 64, 2, 2])
 K2B_EXPORT int k2_int4_qk_norm_rope(void* a, void* w, void* xs, void* ws, void* norm, void* freqs, void* output, int m,
                                     int n, int k, int dtype, float eps, void* stream) {
-  if (dtype != 0 || n % 256) return (int)cudaErrorInvalidValue;
+  if (dtype != 0 || n % 128) return (int)cudaErrorInvalidValue;
   SegDesc d = {SEG_QKNORM, n, w, ws, output, n, static_cast<const float*>(norm), eps, nullptr, nullptr, nullptr};
   return gemm_launch(a, xs, m, k, &d, 1, m, static_cast<const float*>(freqs), nullptr, nullptr, (cudaStream_t)stream);
 }

@@ -54,4 +54,36 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   }
 }
 
+// Gated residual of a reduced fp32 projection (the tensor-parallel tail of
+// the out- and down-projections, the same rounding as the GEMM's
+// SEG_RESIDUAL epilogue): out = bf16(r + bf16(bf16(p) * gate[latent])),
+// latent = (base_row + row) / length.  8 columns per thread, n % 8 == 0.
+__global__ void gated_add_kernel(const float* __restrict__ p, const __nv_bfloat16* __restrict__ gate,
+                                 const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ out, int base_row,
+                                 int rows, int n, int length) {
+  const int per_row = n / 8;
+  const int64_t total = (int64_t)rows * per_row;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int row = (int)(i / per_row), c = (int)(i % per_row) * 8;
+    const int64_t off = (int64_t)row * n + c;
+    const float4 p0 = __ldg(reinterpret_cast<const float4*>(p + off));
+    const float4 p1 = __ldg(reinterpret_cast<const float4*>(p + off + 4));
+    const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(gate + (int64_t)((base_row + row) / length) * n + c));
+    const uint4 r4 = __ldg(reinterpret_cast<const uint4*>(r + off));
+    const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g4);
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&r4);
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 gf = __bfloat1622float2(g2[j]), rf = __bfloat1622float2(r2[j]);
+      const float x0 = bf16_round(__fmul_rn(bf16_round(pv[2 * j]), gf.x));
+      const float x1 = bf16_round(__fmul_rn(bf16_round(pv[2 * j + 1]), gf.y));
+      w[j] = pack_bf16x2(__fadd_rn(rf.x, x0), __fadd_rn(rf.y, x1));
+    }
+    *reinterpret_cast<uint4*>(out + off) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 }  // namespace k2b

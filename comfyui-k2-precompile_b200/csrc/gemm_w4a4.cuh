@@ -203,6 +203,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   // SwiGLU tiles pair 128 gate rows (map 0) with the same 128 up rows (map 1).
   const bool pairw = (S.kind == SEG_SWIGLU || S.kind == SEG_SWIGLU_BF16);
   const int n0 = tile * (pairw ? GEMM_BN / 2 : GEMM_BN);
+  // A segment may end half way through its last tile (width a multiple of
+  // 128): the weight rows beyond it are zero-filled by TMA, only the valid
+  // scales are copied and the epilogue stores no column past the end.
+  const int vcols = pairw ? GEMM_BN : min(GEMM_BN, S.n - n0);
   const int G = p.G;
 
   if (threadIdx.x == 0) {
@@ -270,7 +274,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (chunk >= 2 && !mbar_wait(&empty_sc[cb], ((chunk >> 1) & 1) ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
             const int g0 = chunk * GEMM_SC_GROUPS;
             const int ng = min(GEMM_SC_GROUPS, G - g0);
-            mbar_arrive_expect_tx(&full_sc[cb], ng * GEMM_BN * 4);
+            mbar_arrive_expect_tx(&full_sc[cb], ng * (pairw ? GEMM_BN : vcols) * 4);
             uint8_t* dst = smem + GEMM_OFF_SC + cb * GEMM_SC_BYTES;
             for (int j = 0; j < ng; ++j) {
               const int64_t off = (int64_t)(g0 + j) * S.n + n0;
@@ -278,7 +282,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 2, &full_sc[cb]);
                 bulk_load(dst + j * GEMM_BN * 4 + GEMM_BN * 2, S.wscale2 + off, GEMM_BN * 2, &full_sc[cb]);
               } else {
-                bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 4, &full_sc[cb]);
+                bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, (uint32_t)vcols * 4u, &full_sc[cb]);
               }
             }
             issued_sc = chunk + 1;
@@ -455,15 +459,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     float* xch = reinterpret_cast<float*>(smem + GEMM_OFF_W);
     if (ok) {
       const int col0 = n0 + cq * 64;  // first segment column of this thread (non-SwiGLU kinds)
+      const bool col_ok = pairw || col0 < S.n;
       if (S.kind == SEG_F32) {
-        if (row_ok) {
+        if (row_ok && col_ok) {
           float* o = reinterpret_cast<float*>(S.out) + (int64_t)row * S.ld + col0;
 #pragma unroll
           for (int i = 0; i < 64; i += 4)
             *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
         }
       } else if (S.kind == SEG_BF16 || S.kind == SEG_SIGMOID) {
-        if (row_ok) {
+        if (row_ok && col_ok) {
           if (S.kind == SEG_SIGMOID) {
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[i] = sigmoid_contract(bf16_round(acc[i]));
@@ -471,7 +476,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           store_bf16x64(reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + col0, acc);
         }
       } else if (S.kind == SEG_RESIDUAL) {
-        if (row_ok) {
+        if (row_ok && col_ok) {
           const int bidx = row / p.length;
           const __nv_bfloat16* gt = p.gate + (int64_t)bidx * S.n + col0;
           const __nv_bfloat16* rs = p.resid + (int64_t)row * S.ld + col0;
@@ -525,7 +530,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         epi_barrier();
         const float inv = pbuf[16];
-        if (row_ok) {
+        if (row_ok && col_ok) {
           const int token = row % p.length;
           const int hc0 = (cq & 1) * 64;  // column of this thread's first value within the head
           const float* f = p.freqs + (int64_t)token * 256 + 2 * hc0;

@@ -76,8 +76,9 @@ static int launch_status() { return (int)cudaGetLastError(); }
 // ----------------------------------------------------------- norm_quant
 template <bool NORM, bool MOD, bool QUANT>
 static int norm_quant_launch(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
-                             int rows, int K, int length, int cut, int batch, float eps, cudaStream_t st) {
-  if (rows <= 0 || K <= 0 || K % 512 || K > 16384 || (MOD && (length <= 0 || batch <= 0)))
+                             int rows, int K, int length, int cut, int batch, float eps, cudaStream_t st,
+                             int base_row = 0) {
+  if (rows <= 0 || K <= 0 || K % 512 || K > 16384 || (MOD && (length <= 0 || batch <= 0)) || base_row < 0)
     return (int)cudaErrorInvalidValue;
   if (!aligned16(x) || !aligned16(q) || (QUANT && !s) || (NORM && !aligned16(w)) ||
       (MOD && (!aligned16(scale) || !aligned16(shift))))
@@ -104,7 +105,7 @@ static int norm_quant_launch(const void* x, const void* w, const void* scale, co
   norm_quant_kernel<NORM, MOD, QUANT><<<grid, kNqThreads, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(w), static_cast<const __nv_bfloat16*>(scale),
       static_cast<const __nv_bfloat16*>(shift), static_cast<uint8_t*>(q), static_cast<__half*>(s), rows, K, length,
-      cut, batch, eps);
+      cut, batch, eps, base_row);
   return launch_status();
 }
 
@@ -158,8 +159,10 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     const SegDesc& d = segs[i];
     const bool pairw = d.kind == SEG_SWIGLU || d.kind == SEG_SWIGLU_BF16;
     if (pairw && nseg != 1) return (int)cudaErrorInvalidValue;
+    // SwiGLU pairs 128 gate + 128 up columns per tile; other segments take
+    // any multiple of 128 columns (a last tile may be half used)
     const int tile_n = pairw ? GEMM_BN / 2 : GEMM_BN;
-    if (d.n <= 0 || d.n % tile_n || !aligned16(d.w) || !aligned16(d.wscale) || !d.out) return (int)cudaErrorInvalidValue;
+    if (d.n <= 0 || d.n % 128 || !aligned16(d.w) || !aligned16(d.wscale) || !d.out) return (int)cudaErrorInvalidValue;
     // each CTA of a pair loads 128 weight rows per K group
     int rc = make_map_2d(&wm.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w, (uint64_t)K, (uint64_t)d.n, (uint64_t)K,
                          128, GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -171,7 +174,7 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
       if (rc) return rc;
     }
     GemmSegment& g = p.seg[i];
-    g.tiles = d.n / tile_n;
+    g.tiles = (d.n + tile_n - 1) / tile_n;
     g.kind = d.kind;
     g.n = d.n;
     g.ld = d.ld;
@@ -315,6 +318,17 @@ K2B_EXPORT int k2b_norm_quant(const void* x, const void* w, const void* scale, c
                                              (cudaStream_t)stream);
 }
 
+// norm_quant of rows [base_row, base_row + rows) of a latent stream (x, q, s
+// point at the first of them): the modulation row of each row follows its
+// index in the whole stream, so a row shard quantises exactly as the
+// unsharded call would.
+K2B_EXPORT int k2b_norm_quant_rows(const void* x, const void* w, const void* scale, const void* shift, void* q,
+                                   void* s, int base_row, int rows, int K, int length, int cut, int batch, float eps,
+                                   void* stream) {
+  return norm_quant_launch<true, true, true>(x, w, scale, shift, q, s, rows, K, length, cut, batch, eps,
+                                             (cudaStream_t)stream, base_row);
+}
+
 K2B_EXPORT int k2b_rotate_quant(const void* x, void* q, void* s, int rows, int K, void* stream) {
   return norm_quant_launch<false, false, true>(x, nullptr, nullptr, nullptr, q, s, rows, K, 1, -1, 1, 0.0f,
                                                (cudaStream_t)stream);
@@ -328,6 +342,21 @@ K2B_EXPORT int k2b_norm_mod(const void* x, const void* w, const void* scale, con
                                                 (cudaStream_t)stream);
   return norm_quant_launch<true, false, false>(x, w, nullptr, nullptr, y, nullptr, rows, K, 1, -1, 1, eps,
                                                (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_gated_add(const void* p, const void* gate, const void* resid, void* out, int base_row, int rows,
+                             int n, int length, void* stream) {
+  if (rows < 0 || n <= 0 || n % 8 || length <= 0 || base_row < 0 || !aligned16(p) || !aligned16(gate) ||
+      !aligned16(resid) || !aligned16(out))
+    return (int)cudaErrorInvalidValue;
+  if (rows == 0) return 0;
+  const long long work = (long long)rows * (n / 8);
+  const long long blocks = (work + 255) / 256;
+  const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
+  gated_add_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const float*>(p), static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(resid),
+      static_cast<__nv_bfloat16*>(out), base_row, rows, n, length);
+  return launch_status();
 }
 
 K2B_EXPORT int k2b_elementwise(const void* a, const void* b, const void* r, void* y, long long n, int mode, int width,
@@ -386,7 +415,7 @@ K2B_EXPORT int k2b_qkv(const void* a, const void* sa, const void* wq, const void
                        const void* swk, const void* wv, const void* swv, const void* wg, const void* swg,
                        const void* nq, const void* nk, const void* freqs, void* qo, void* ko, void* vo, void* go,
                        int m, int length, int qwidth, int kvwidth, int k, float eq, float ek, void* stream) {
-  if (qwidth % 256 || kvwidth % 256) return (int)cudaErrorInvalidValue;
+  if (qwidth <= 0 || kvwidth <= 0 || qwidth % 128 || kvwidth % 128) return (int)cudaErrorInvalidValue;
   SegDesc d[4] = {
       {SEG_QKNORM, qwidth, wq, swq, qo, qwidth, static_cast<const float*>(nq), eq, nullptr, nullptr, nullptr},
       {SEG_QKNORM, kvwidth, wk, swk, ko, kvwidth, static_cast<const float*>(nk), ek, nullptr, nullptr, nullptr},

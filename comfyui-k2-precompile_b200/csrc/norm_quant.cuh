@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
                                                                 const __nv_bfloat16* __restrict__ shift,
                                                                 uint8_t* __restrict__ q, __half* __restrict__ s,
                                                                 int rows, int K, int length, int cut, int batch,
-                                                                float eps) {
+                                                                float eps, int base_row) {
   __shared__ float s_inv[kNqRows];
   __shared__ int s_lat[kNqRows];  // modulation row (latent) of each tile row
   __shared__ __align__(16) float s_tr[4][4 * kNqGroupFloats];
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
         if (lane == 0) {
           s_inv[r] = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), eps));
           if constexpr (MOD) {
-            const int row = row0 + r;
+            const int row = base_row + row0 + r;  // row index within the latent stream
             int bb = row / length;
             if (cut >= 0 && row % length >= cut) bb += batch;
             s_lat[r] = bb;

@@ -18,7 +18,7 @@ from __future__ import annotations
 import ctypes
 import math
 from dataclasses import dataclass, field
-from typing import List, Optional
+from typing import Callable, List, Optional, Tuple
 
 import torch
 
@@ -101,8 +101,12 @@ def _norm_weight(n: int, gen: torch.Generator, device) -> torch.Tensor:
     return (w_eff.to(torch.float32) - 1.0).contiguous()
 
 
-def synthetic_blocks(cfg: ModelConfig, batch: int, seed: int = 0, device="cuda", keep_packed: bool = False
-                     ) -> List[BlockWeights]:
+def synthetic_blocks(cfg: ModelConfig, batch: int, seed: int = 0, device="cuda", keep_packed: bool = False,
+                     shard: Optional[Callable[[str, torch.Tensor, torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]]
+                     = None) -> List[BlockWeights]:
+    """``shard(name, packed, scales)`` (optional) keeps a slice of each packed
+    weight before it is prepared: every rank draws the same full weights from
+    the seed and keeps its own shard (k2b.parallel.shard_packed)."""
     gen = torch.Generator(device=device).manual_seed(seed)
     H, D = cfg.hidden, cfg.head_dim
     shapes = {"wq": (cfg.heads * D, H), "wk": (cfg.kvheads * D, H), "wv": (cfg.kvheads * D, H),
@@ -114,6 +118,8 @@ def synthetic_blocks(cfg: ModelConfig, batch: int, seed: int = 0, device="cuda",
             w = (torch.randn((n, k), generator=gen, device=device) * 0.02).to(torch.bfloat16)
             q, s = quantize_weight(w)
             del w
+            if shard is not None:
+                q, s = shard(name, q, s)
             prepared[name] = ops.prepare_weight(q, s)
             if keep_packed:
                 packed[name] = (q, s)

@@ -108,6 +108,55 @@ def norm_quant(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: tor
     return q, s
 
 
+def norm_quant_rows(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, *,
+                    base_row: int, length: int, batch: int, cut: int = -1, eps: float = 1e-6,
+                    out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """norm_quant of rows [base_row, base_row + rows) of a stream of ``batch``
+    latents of ``length`` rows: x bf16 [rows, K] holds just those rows, and the
+    modulation row of each follows its index in the whole stream.  ``out``
+    (q, s) may name views to write into (e.g. this rank's slot of an
+    all-gather buffer)."""
+    _cuda(x, w, scale, shift)
+    _need(x.dtype == torch.bfloat16 and scale.dtype == torch.bfloat16 and shift.dtype == torch.bfloat16 and
+          w.dtype == torch.float32, "norm_quant_rows: bf16 x/modulation, fp32 w expected")
+    K = int(x.shape[-1])
+    rows = x.numel() // K
+    _need(base_row >= 0 and base_row + rows <= batch * length, "norm_quant_rows: rows outside the stream")
+    _need(w.numel() == K and scale.shape[-1] == K and shift.numel() == scale.numel() and
+          scale.numel() // K >= (2 * batch if cut >= 0 else batch), "norm_quant_rows: modulation shape")
+    if out is None:
+        q = torch.empty((rows, K // 2), dtype=torch.uint8, device=x.device)
+        s = torch.empty((rows, K // GROUP), dtype=torch.float16, device=x.device)
+    else:
+        q, s = out
+        _cuda(q, s)
+        _need(q.dtype == torch.uint8 and s.dtype == torch.float16 and q.numel() == rows * K // 2 and
+              s.numel() == rows * K // GROUP, "norm_quant_rows: output shapes")
+    if rows:
+        check(lib().k2b_norm_quant_rows(_p(x), _p(w), _p(scale), _p(shift), _p(q), _p(s), base_row, rows, K, length,
+                                        cut, batch, ctypes.c_float(eps), _stream()), "k2b_norm_quant_rows")
+    return q, s
+
+
+def gated_add(p: torch.Tensor, gate: torch.Tensor, residual: torch.Tensor, *, base_row: int, length: int,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = bf16(residual + bf16(bf16(p) * gate[(base_row + row) // length]))
+    for a reduced fp32 projection p [rows, n] (k2b_gated_add)."""
+    _cuda(p, gate, residual, out)
+    _need(p.dtype == torch.float32 and gate.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16,
+          "gated_add: fp32 p, bf16 gate/residual expected")
+    n = int(p.shape[-1])
+    rows = p.numel() // n
+    _need(residual.numel() == rows * n and gate.shape[-1] == n, "gated_add: shapes")
+    _need(rows == 0 or (base_row + rows - 1) // length < gate.numel() // n, "gated_add: gate rows do not cover")
+    if out is None:
+        out = torch.empty((rows, n), dtype=torch.bfloat16, device=p.device)
+    _need(out.dtype == torch.bfloat16 and out.numel() == rows * n, "gated_add: out shape")
+    check(lib().k2b_gated_add(_p(p), _p(gate), _p(residual), _p(out), base_row, rows, n, length, _stream()),
+          "k2b_gated_add")
+    return out
+
+
 def norm_mod(x: torch.Tensor, w: torch.Tensor, scale: Optional[torch.Tensor] = None,
              shift: Optional[torch.Tensor] = None, *, length: Optional[int] = None, cut: int = -1,
              eps: float = 1e-6) -> torch.Tensor:
@@ -183,10 +232,15 @@ def _act(a: torch.Tensor, sa: torch.Tensor, k: int) -> int:
     return int(a.shape[0])
 
 
-def gemm_f32(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Tensor:
-    _cuda(a, sa, W.w, W.scale)
+def gemm_f32(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, out: Optional[torch.Tensor] = None
+             ) -> torch.Tensor:
+    """fp32 a@W (exact group accumulation); ``out`` may be a preallocated
+    [m, n] fp32 buffer (e.g. the first rows of a reduce-scatter input)."""
+    _cuda(a, sa, W.w, W.scale, out)
     m = _act(a, sa, W.k)
-    out = torch.empty((m, W.n), dtype=torch.float32, device=a.device)
+    if out is None:
+        out = torch.empty((m, W.n), dtype=torch.float32, device=a.device)
+    _need(out.dtype == torch.float32 and out.dim() == 2 and tuple(out.shape) == (m, W.n), "gemm_f32: out shape")
     check(lib().k2b_gemm_f32(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
           "k2b_gemm_f32")
     return out
@@ -316,7 +370,7 @@ def device_error(reset: bool = True) -> int:
 
 
 __all__ = [
-    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_mod", "elementwise", "rope", "rotate_quant",
+    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_quant_rows", "gated_add", "norm_mod", "elementwise", "rope", "rotate_quant",
     "gemm_f32", "gemm_bf16", "qkv",
     "gated_residual", "swiglu_quant", "swiglu_bf16", "attention", "attention_quant", "device_error",
 ]

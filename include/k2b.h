@@ -55,6 +55,13 @@ int k2b_device_error(int reset, void* stream);
 int k2b_norm_quant(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                    int rows, int K, int length, int cut, int batch, float eps, void* stream);
 
+/* k2b_norm_quant of rows [base_row, base_row+rows) of a latent stream (x, q,
+ * s point at the first of them): the modulation row follows the row's index
+ * in the whole stream, so a row shard of a tensor-parallel group quantises
+ * exactly as the unsharded call. */
+int k2b_norm_quant_rows(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
+                        int base_row, int rows, int K, int length, int cut, int batch, float eps, void* stream);
+
 /* H128 rotation + group-128 INT4 of a bf16 activation: the input quantisation
  * `quantize()` performs before an INT4 projection (native_runtime.cpp:268-271;
  * comfy-kitchen quantize_int4_rowwise_convrot64 via k2_quant4,
@@ -92,7 +99,7 @@ int k2b_prepare_weight(const void* w_packed, const void* w_scale, void* w_prepar
                        int block_rows, int dst_block_stride, int dst_offset, int scale_ld, void* stream);
 
 /* -------------------------------------------------------------- W4A4 GEMM --
- * a u8 [m,k/2] + sa fp16 [m,k/128]; w/wscale prepared; n % 256 == 0. */
+ * a u8 [m,k/2] + sa fp16 [m,k/128]; w/wscale prepared; n % 128 == 0. */
 /* fp32 result p (exact group accumulation; k2b's test hook for the int32
  * accumulators). */
 int k2b_gemm_f32(const void* a, const void* sa, const void* w, const void* wscale, void* out, int m, int n, int k,
@@ -108,7 +115,7 @@ int k2b_gemm_bf16(const void* a, const void* sa, const void* w, const void* wsca
  * freqs fp32 [length,64,2,2] (token = row % length); V: bf16(p);
  * gate (optional, wg/go non-null): bf16(sigmoid(bf16(p))).
  * Outputs token-major bf16: qo [m,qwidth], ko/vo [m,kvwidth], go [m,qwidth].
- * qwidth, kvwidth multiples of 256. */
+ * qwidth, kvwidth multiples of 128. */
 int k2b_qkv(const void* a, const void* sa, const void* wq, const void* swq, const void* wk, const void* swk,
             const void* wv, const void* swv, const void* wg, const void* swg, const void* nq, const void* nk,
             const void* freqs, void* qo, void* ko, void* vo, void* go, int m, int length, int qwidth, int kvwidth,
@@ -120,6 +127,13 @@ int k2b_qkv(const void* a, const void* sa, const void* wq, const void* swq, cons
  * output half of k2_int4_residual_norm (kernels/joint_projection.cu:178-179). */
 int k2b_gated_residual(const void* a, const void* sa, const void* w, const void* wscale, const void* gate,
                        const void* residual, void* out, int m, int length, int n, int k, void* stream);
+
+/* The gated residual applied to an already reduced fp32 projection p
+ * [rows, n] (the tail of a tensor-parallel out/down projection after its
+ * reduce-scatter): out = bf16(resid + bf16(bf16(p)*gate[(base_row+row)/length])),
+ * the rounding of k2b_gated_residual.  n % 8 == 0. */
+int k2b_gated_add(const void* p, const void* gate, const void* resid, void* out, int base_row, int rows, int n,
+                  int length, void* stream);
 
 /* Gate/up projection + SwiGLU + INT4 requant of the down-projection input:
  * h = bf16(bf16(silu(bf16(pg)))*bf16(pu)), then H128 rotation + group-128
