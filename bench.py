@@ -490,12 +490,15 @@ def main():
         x.copy_(x0)
         wl.step(x)
     torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
+    # the sampler starts before the barrier: a rank that enters the timed
+    # region while rank 0 still waits for nvidia-smi would time that wait at
+    # its first collective
     sampler = ClockSampler([local_rank] if world == 1 else range(world)) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for i in range(args.steps):

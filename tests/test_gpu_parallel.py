@@ -105,7 +105,7 @@ def test_tp_lockstep_matches_native_block_loop(cuda, tp, batch, length):
     from k2b.model import Krea2Blocks, ModelConfig, rope_positions, rope_table, synthetic_blocks
     from k2b.parallel import run_lockstep
 
-    cfg = ModelConfig(hidden=1024, heads=16, kvheads=4, mlp=2048, blocks=2)
+    cfg = ModelConfig(hidden=1024, heads=8, kvheads=4, mlp=2048, blocks=2)
     full = Krea2Blocks(cfg, synthetic_blocks(cfg, batch, seed=3, device=cuda), batch, length, device=cuda)
     side = 12
     freqs = rope_table(rope_positions(length - (length // side) * side, length // side, side), (64, 64)).to(cuda)
@@ -143,7 +143,7 @@ def _nccl_rank(rank, world, port, path):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     try:
-        cfg = ModelConfig(hidden=1024, heads=16, kvheads=4, mlp=2048, blocks=2)
+        cfg = ModelConfig(hidden=1024, heads=8, kvheads=4, mlp=2048, blocks=2)
         batch, length = 2, 150
         topo = topology(world, rank, world)
         plan = TPPlan.of(cfg, world, rank)
@@ -178,7 +178,7 @@ def test_tp2_nccl_matches_native_block_loop(cuda, tmp_path):
     path = str(tmp_path / "tp")
     mp.start_processes(_nccl_rank, args=(2, port, path), nprocs=2, start_method="spawn")
     got = np.concatenate([np.load(f"{path}.{r}.npy") for r in range(2)], 0)
-    cfg = ModelConfig(hidden=1024, heads=16, kvheads=4, mlp=2048, blocks=2)
+    cfg = ModelConfig(hidden=1024, heads=8, kvheads=4, mlp=2048, blocks=2)
     batch, length = 2, 150
     full = Krea2Blocks(cfg, synthetic_blocks(cfg, batch, seed=3, device=cuda), batch, length, device=cuda)
     freqs = rope_table(rope_positions(6, 12, 12), (64, 64)).to(cuda)
