@@ -35,7 +35,9 @@
 // of group g+1 overlaps the dequant of group g.  The fp32 group sum lives in
 // the epilogue registers (64 per thread); TMEM loads are software-pipelined
 // one 16-column chunk ahead.  setmaxnreg gives the TMA/MMA/unpack warpgroup
-// 32 registers and the four epilogue warpgroups 112.
+// 32 registers and the four epilogue warpgroups 112.  For SwiGLU a thread
+// owns 32 gate and the same 32 up columns (its 32 output columns), so the
+// final SwiGLU + rotation + requant is spread over all 16 epilogue warps.
 //
 // Dequant contract (oracle: k2o_gemm_w4a4):
 //   p = 0;  for g:  u = fp32(acc_g * sA[r,g]);  p = fmaf(u, sW[c,g], p)
@@ -43,7 +45,9 @@
 // half of each byte), so the TMEM accumulator is x = 256*acc_g (|x| <= 2^21).
 // The epilogue turns it into fp32 with an integer add of the exponent bias
 // (bits 0x4B400000 + x read as the float 12582912 + x, exactly) and removes
-// the bias inside the first fma:
+// the bias inside the first fma.  (Seeding the accumulator with the bias
+// instead, so the add disappears, costs a TMEM store pass per group and was
+// measured slower.)
 //   u = fma(12582912 + x, sA/256, -12582912*sA/256) = fp32(acc_g * sA)
 // (both sA/256 and 12582912*sA/256 are exact for an fp16-valued sA).
 #pragma once
@@ -77,8 +81,10 @@ constexpr int GEMM_OFF_BAR = GEMM_OFF_SC + 2 * GEMM_SC_BYTES;
 constexpr int GEMM_NBARS = 2 * GEMM_STAGES + 2 * GEMM_PSTAGES + 2 * 2 + 4;
 constexpr int GEMM_SMEM_BYTES = GEMM_OFF_BAR + GEMM_NBARS * 8 + 16 + 1024;  // + alignment slack
 // The final epilogue exchanges rows through the (then idle) W, unpacked-A and
-// packed-A stages: SwiGLU needs 2*128*65 + 2*128*66 floats.
-static_assert(GEMM_OFF_SC >= (2 * 128 * 65 + 2 * 128 * 66) * 4, "exchange space");
+// packed-A stages: SwiGLU needs two 4 x 128 x 33-float stage buffers and 512
+// floats for the group maxima.
+constexpr int kSwXch = 4 * 128 * 33;
+static_assert(GEMM_OFF_SC >= (2 * kSwXch + 512) * 4, "exchange space");
 // Accumulator seed: as fp32 bits, 0x4B400000 + x reads as 12582912 + x for |x| < 2^22.
 constexpr uint32_t kAccBias = 0x4B400000u;
 
@@ -158,6 +164,9 @@ __device__ __forceinline__ void store_bf16x64(__nv_bfloat16* o, const float (&v)
   }
 }
 
+// PAIRW: SwiGLU launches (one segment of gate/up column pairs); the column
+// mapping of the epilogue threads is then a compile-time choice.
+template <bool PAIRW>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w4a4_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ WeightMaps wmaps,
                      const __grid_constant__ GemmParams p) {
@@ -201,7 +210,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
   const GemmSegment& S = p.seg[seg];
   // SwiGLU tiles pair 128 gate rows (map 0) with the same 128 up rows (map 1).
-  const bool pairw = (S.kind == SEG_SWIGLU || S.kind == SEG_SWIGLU_BF16);
+  constexpr bool pairw = PAIRW;  // the launcher checks S.kind against it
   const int n0 = tile * (pairw ? GEMM_BN / 2 : GEMM_BN);
   // A segment may end half way through its last tile (width a multiple of
   // 128): the weight rows beyond it are zero-filled by TMA, only the valid
@@ -365,10 +374,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int row = m0 + rloc;
     const bool row_ok = row < p.M;
     const __half* sa_row = p.sa + (int64_t)(row_ok ? row : 0) * G;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + cq * 64;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    // This thread's TMEM / scale columns: chunks ca, ca+16, cb, cb+16 land in
+    // register slots 0, 16, 32, 48.  SwiGLU: 32 gate columns (ca) and the same
+    // 32 up columns (cb = 128 + ca); other kinds: 64 consecutive columns.
+    // ca: first column; chunk offsets 0, 16, kCd, kCd + 16 from ca
+    constexpr int kCd = pairw ? GEMM_BN / 2 : 32;
+    const int ca = pairw ? 32 * cq : 64 * cq;
+    const int cb = ca + kCd;
     const uint32_t tmem_empty_remote = cluster_map(smem_u32(tmem_empty), 0);
     bool ok = true;
-    float2 acc2[32];  // columns (2j, 2j+1)
+    float2 acc2[32];  // register slots (2j, 2j+1)
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc2[j] = make_float2(0.0f, 0.0f);
     // TMEM loads are software-pipelined: the load of chunk c+1 (16 columns)
@@ -379,43 +395,44 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t s_full_sc = smem_u32(full_sc), s_empty_sc = smem_u32(empty_sc);
     const uint32_t s_tfull = smem_u32(tmem_full), s_tempty = smem_u32(tmem_empty);
     const uint32_t s_abort = smem_u32((const void*)abort_flag);
-    const uint32_t s_scales = smem_u32(smem + GEMM_OFF_SC) + cq * 64 * 4;
-    auto dequant16 = [&](const uint32_t (&v)[16], uint32_t scs, int c0, float2 sa2, float2 sb2) {
+    const uint32_t s_scales = smem_u32(smem + GEMM_OFF_SC) + 4 * ca;
+    auto dequant16 = [&](const uint32_t (&v)[16], uint32_t scs, int slot0, float2 sa2, float2 sb2) {
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
-        const float4 sw = lds128(scs + 4 * (c0 + i));  // scales of columns c0+i .. +3
+        const float4 sw = lds128(scs + 4 * i);  // scales of this chunk's columns i .. i+3
         const float2 u0 = __ffma2_rn(
             make_float2(__uint_as_float(v[i] + kAccBias), __uint_as_float(v[i + 1] + kAccBias)), sa2, sb2);
         const float2 u1 = __ffma2_rn(
             make_float2(__uint_as_float(v[i + 2] + kAccBias), __uint_as_float(v[i + 3] + kAccBias)), sa2, sb2);
-        acc2[(c0 + i) / 2] = __ffma2_rn(u0, make_float2(sw.x, sw.y), acc2[(c0 + i) / 2]);
-        acc2[(c0 + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(c0 + i) / 2 + 1]);
+        acc2[(slot0 + i) / 2] = __ffma2_rn(u0, make_float2(sw.x, sw.y), acc2[(slot0 + i) / 2]);
+        acc2[(slot0 + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(slot0 + i) / 2 + 1]);
       }
     };
+    const uint32_t tcol = lane_base + ca;  // this thread's first column in buffer 0
     uint32_t va[16], vb[16];
     ok = mbar_wait_s(s_full_sc, 0, s_abort, ERR_WAIT_EPILOGUE) && mbar_wait_s(s_tfull, 0, s_abort, ERR_WAIT_EPILOGUE);
     if (ok) {
       tc_fence_after();
-      tmem_ld16(lane_base, va);
+      tmem_ld16(tcol, va);
     }
     __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
     for (int g = 0; g < G && ok; ++g) {
-      const int b = g & 1, cb = (g / GEMM_SC_GROUPS) & 1;
+      const int b = g & 1, cbuf = (g / GEMM_SC_GROUPS) & 1;
       const float sa = row_ok ? __fmul_rn(__half2float(sa_next), 0.00390625f) : 0.0f;
       if (g + 1 < G) sa_next = sa_row[g + 1];
       const float sbias = __fmul_rn(sa, -12582912.0f);
       const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sbias, sbias);
-      const uint32_t scs = s_scales + cb * GEMM_SC_BYTES + (g % GEMM_SC_GROUPS) * GEMM_BN * 4;
-      const uint32_t taddr = lane_base + b * GEMM_BN;
+      const uint32_t scs = s_scales + cbuf * GEMM_SC_BYTES + (g % GEMM_SC_GROUPS) * GEMM_BN * 4;
+      const uint32_t taddr = tcol + b * GEMM_BN;
       tmem_wait_ld_regs(va);
       tmem_ld16(taddr + 16, vb);
       dequant16(va, scs, 0, sa2, sb2);
       tmem_wait_ld_regs(vb);
-      tmem_ld16(taddr + 32, va);
-      dequant16(vb, scs, 16, sa2, sb2);
+      tmem_ld16(taddr + kCd, va);
+      dequant16(vb, scs + 64, 16, sa2, sb2);
       tmem_wait_ld_regs(va);
-      tmem_ld16(taddr + 48, vb);
-      dequant16(va, scs, 32, sa2, sb2);
+      tmem_ld16(taddr + kCd + 16, vb);
+      dequant16(va, scs + 4 * kCd, 32, sa2, sb2);
       tmem_wait_ld_regs(vb);
       // every column of group g is in registers: hand the buffer back to the MMA
       tc_fence_before();
@@ -431,15 +448,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
              mbar_wait_s(s_full_sc + 8u * (uint32_t)(c1 & 1), (c1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) &&
             mbar_wait_s(s_tfull + 8u * (uint32_t)(g1 & 1), (g1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) {
           tc_fence_after();
-          tmem_ld16(lane_base + (g1 & 1) * GEMM_BN, va);
+          tmem_ld16(tcol + (g1 & 1) * GEMM_BN, va);
         } else {
           ok = false;
         }
       }
-      dequant16(vb, scs, 48, sa2, sb2);
+      dequant16(vb, scs + 4 * kCd + 64, 48, sa2, sb2);
       __syncwarp();
       if (lane == 0 && (g % GEMM_SC_GROUPS == GEMM_SC_GROUPS - 1 || g == G - 1))
-        mbar_arrive_s(s_empty_sc + 8u * (uint32_t)cb);
+        mbar_arrive_s(s_empty_sc + 8u * (uint32_t)cbuf);
     }
     if (!ok) tmem_wait_ld();  // no TMEM load stays in flight
 
@@ -553,71 +570,77 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       } else if (pairw) {
-        // Quarters 0/1 hold gate columns 0-63 / 64-127 of the 128 output
-        // columns, quarters 2/3 the up columns; the up quarters hand bf16(up)
-        // to their gate partner through shared memory.
-        const int h = cq & 1;  // which 64-column half of the output group
-        float* ubuf = xch + (h * 128 + rloc) * 65;
-        if (cq >= 2) {
+        // acc[0..31]: gate, acc[32..63]: up of output columns 32*cq .. +31 of
+        // this tile's 128 (SwiGLU rounding of kernels/joint_projection.cu:94-97).
+        float hv[32];
 #pragma unroll
-          for (int i = 0; i < 64; ++i) ubuf[i] = bf16_round(acc[i]);
-        }
-        epi_barrier();
-        if (cq < 2) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float gv = bf16_round(acc[i]);
-            const float av = bf16_round(silu_contract(gv));
-            acc[i] = bf16_round(__fmul_rn(av, ubuf[i]));
-          }
+        for (int i = 0; i < 32; ++i) {
+          const float gv = bf16_round(acc[i]);
+          const float av = bf16_round(silu_contract(gv));
+          hv[i] = bf16_round(__fmul_rn(av, bf16_round(acc[32 + i])));
         }
         if (S.kind == SEG_SWIGLU_BF16) {
-          if (cq < 2 && row_ok)
-            store_bf16x64(reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + n0 + h * 64, acc);
+          if (row_ok) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out) + (int64_t)row * S.ld + n0 + 32 * cq;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(o + i) =
+                  make_uint4(pack_bf16x2(hv[i], hv[i + 1]), pack_bf16x2(hv[i + 2], hv[i + 3]),
+                             pack_bf16x2(hv[i + 4], hv[i + 5]), pack_bf16x2(hv[i + 6], hv[i + 7]));
+          }
         } else {
-          // H128 over the pair: stages 1..32 inside each half, stage 64 across.
-          float* hbuf = xch + 2 * 128 * 65 + (h * 128 + rloc) * 66;
-          const float* other = xch + 2 * 128 * 65 + ((h ^ 1) * 128 + rloc) * 66;
-          if (cq < 2) {
-            hadamard64_regs(acc);
+          // H128 of the row's 128 outputs, held 32 per thread by the four
+          // column quarters: stages 2, 4, 8, 1, 16 in registers, then 32
+          // (partner quarter cq^1) and 64 (cq^2) through shared memory.
 #pragma unroll
-            for (int i = 0; i < 64; ++i) hbuf[i] = acc[i];
+          for (int st = 0; st < 5; ++st) {
+            const int lh = hadamard_stage_bit(st);
+            const int h = 1 << lh;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int lo = ((i >> lh) << (lh + 1)) | (i & (h - 1));
+              const float x0 = hv[lo], x1 = hv[lo + h];
+              hv[lo] = __fadd_rn(x0, x1);
+              hv[lo + h] = __fsub_rn(x0, x1);
+            }
           }
-          epi_barrier();
+#pragma unroll
+          for (int xs = 0; xs < 2; ++xs) {
+            const int bit = 1 << xs;  // partner quarter cq ^ bit: output distance 32 << xs
+            float* mine = xch + xs * kSwXch + (cq * 128 + rloc) * 33;
+            const float* other = xch + xs * kSwXch + ((cq ^ bit) * 128 + rloc) * 33;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mine[i] = hv[i];
+            epi_barrier();
+            const bool upper = (cq & bit) != 0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float lo = upper ? other[i] : hv[i];
+              const float hi = upper ? hv[i] : other[i];
+              hv[i] = upper ? __fsub_rn(lo, hi) : __fadd_rn(lo, hi);
+            }
+          }
           float amax = 0.0f;
-          if (cq < 2) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-              // element i of the lower half pairs with element i of the upper half
-              const float a = h ? other[i] : acc[i];
-              const float b = h ? acc[i] : other[i];
-              acc[i] = h ? __fsub_rn(a, b) : __fadd_rn(a, b);
-              amax = fmaxf(amax, fabsf(acc[i]));
-            }
-          }
-          epi_barrier();  // both halves have read each other's stage-32 values
-          if (cq < 2) hbuf[64] = amax;
+          for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(hv[i]));
+          float* gmax = xch + 2 * kSwXch + rloc * 4;
+          gmax[cq] = amax;
           epi_barrier();
-          if (cq < 2) {
-            amax = fmaxf(amax, other[64]);
-            const QuantGroup qg = quant_group(amax);
-            const int grp = n0 / 128;  // output group (128 columns) index
-            if (row_ok) {
-              if (h == 0) S.out_scale[(int64_t)row * (S.n / 128) + grp] = qg.scale;
-              uint8_t* o = reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld + grp * 64 + h * 32;
+          amax = fmaxf(fmaxf(gmax[0], gmax[1]), fmaxf(gmax[2], gmax[3]));
+          const QuantGroup qg = quant_group(amax);
+          const int grp = n0 / 128;  // output group (128 columns) index
+          if (row_ok) {
+            if (cq == 0) S.out_scale[(int64_t)row * (S.n / 128) + grp] = qg.scale;
+            uint32_t w[4];
 #pragma unroll
-              for (int i = 0; i < 64; i += 32) {
-                uint32_t w[4];
+            for (int j = 0; j < 4; ++j) {
+              uint32_t bits8[8];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  uint32_t b[8];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) b[e] = quant_bits(acc[i + 8 * j + e], qg.c, qg.clamp);
-                  w[j] = pack8_codes(b);
-                }
-                *reinterpret_cast<uint4*>(o + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
-              }
+              for (int e = 0; e < 8; ++e) bits8[e] = quant_bits(hv[8 * j + e], qg.c, qg.clamp);
+              w[j] = pack8_codes(bits8);
             }
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld + grp * 64 + cq * 16) =
+                make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }

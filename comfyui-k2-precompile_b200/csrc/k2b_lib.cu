@@ -206,20 +206,22 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
   p.freqs = freqs;
   p.gate = static_cast<const __nv_bfloat16*>(gate);
   p.resid = static_cast<const __nv_bfloat16*>(resid);
-  static bool attr_set[64] = {false};
+  const bool pairw = segs[0].kind == SEG_SWIGLU || segs[0].kind == SEG_SWIGLU_BF16;
+  void (*kern)(CUtensorMap, WeightMaps, GemmParams) = pairw ? gemm_w4a4_kernel<true> : gemm_w4a4_kernel<false>;
+  static bool attr_set[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w4a4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
+  if (!attr_set[dev][pairw]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     // setmaxnreg splits exactly the registers the CTA is launched with: any
     // other allocation could leave a warpgroup waiting for registers.
     cudaFuncAttributes fa;
-    e = cudaFuncGetAttributes(&fa, gemm_w4a4_kernel);
+    e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return (int)e;
     if (fa.numRegs != GEMM_LAUNCH_REGS) return (int)cudaErrorInvalidConfiguration;
-    attr_set[dev] = true;
+    attr_set[dev][pairw] = true;
   }
   // CTA pairs along M (cluster 2 x 1 x 1): 256 rows per pair.
   cudaLaunchConfig_t cfg;
@@ -235,7 +237,7 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_w4a4_kernel, amap, wm, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, amap, wm, p);
   if (e != cudaSuccess) return (int)e;
   return launch_status();
 }
