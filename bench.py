@@ -329,7 +329,7 @@ class Workload:
     over this rank's rows of its group's latents, 13 events per block
     (12 phases: 9 kernels and 4 NCCL collectives)."""
 
-    def __init__(self, torch, cfg, topo, dev, latents):
+    def __init__(self, torch, cfg, topo, dev, latents, fused=True):
         from k2b.model import Krea2Blocks, rope_positions, rope_table, synthetic_blocks
         from k2b.parallel import PHASES, TPBlocks, TPPlan, shard_fn
 
@@ -345,7 +345,7 @@ class Workload:
         else:
             plan = TPPlan.of(cfg, topo.tp, topo.tp_rank)
             self.blocks = synthetic_blocks(cfg, latents, seed=1234, device=dev, shard=shard_fn(plan))
-            self.model = TPBlocks(cfg, self.blocks, plan, topo.tp_group, latents, LENGTH, device=dev)
+            self.model = TPBlocks(cfg, self.blocks, plan, topo.tp_group, latents, LENGTH, device=dev, fused=fused)
             self.rows_here = self.model.shard.chunk
             self.phases = PHASES
             self.ev_per_block = len(PHASES)
@@ -405,6 +405,10 @@ def main():
     ap.add_argument("--tp", type=int, default=1,
                     help="KV-head tensor-parallel degree (1, 2, 4); the remaining factor of the world is batch "
                          "sharding (8 GPUs: --tp 4 gives 4-way head TP x 2-way batch)")
+    ap.add_argument("--tp-fused", action="store_true",
+                    help="with --tp: the out/down projections store their fp32 partials straight into the owner "
+                         "rank's buffer over NVLink peer memory (k2b_gemm_f32_scatter) instead of an NCCL "
+                         "reduce-scatter after them")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="profile mode: norm_quant|qkv|out_proj|gate_up|down|attention on one small case")
@@ -451,7 +455,7 @@ def main():
     peaks, peak_kind = measured_peaks()
     int8_tops = int8_peak_tops(torch) if rank == 0 else None
 
-    wl = Workload(torch, cfg, topo, dev, local)
+    wl = Workload(torch, cfg, topo, dev, local, fused=args.tp_fused)
     freqs = wl.freqs
     rows = wl.rows_here
     # this rank's hidden-state rows of its group's latents (whole latents when tp == 1)
@@ -618,7 +622,10 @@ def main():
                 "frac_of_datasheet_4500": kd.get("frac_of_int8_datasheet"),
                 "traffic": traffic,
                 "work_per_launch": work[dom][0], "avg_launch_us": kd["avg_us"]}
-        par = f"batch-shard x{world}" if tp == 1 else f"kv-head TP x{tp} (row-sharded residual) x batch-shard x{topo.dp}"
+        par = f"batch-shard x{world}" if tp == 1 else (
+            f"kv-head TP x{tp} (row-sharded residual; "
+            f"{'GEMM epilogue scatter over NVLink peer memory' if args.tp_fused else 'NCCL reduce-scatter'} + "
+            f"INT4 NCCL all-gather) x batch-shard x{topo.dp}")
         line = {
             "metric": METRIC, "value": value, "unit": "latents/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -644,6 +651,8 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if tp > 1:
+            wl.model.close()
         del wl
         dist.destroy_process_group()
 

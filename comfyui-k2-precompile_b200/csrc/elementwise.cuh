@@ -57,18 +57,26 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 // Gated residual of a reduced fp32 projection (the tensor-parallel tail of
 // the out- and down-projections, the same rounding as the GEMM's
 // SEG_RESIDUAL epilogue): out = bf16(r + bf16(bf16(p) * gate[latent])),
-// latent = (base_row + row) / length.  8 columns per thread, n % 8 == 0.
-__global__ void gated_add_kernel(const float* __restrict__ p, const __nv_bfloat16* __restrict__ gate,
-                                 const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ out, int base_row,
-                                 int rows, int n, int length) {
+// latent = (base_row + row) / length, with p = ((s_0 + s_1) + s_2) + ... the
+// fp32 sum of `nslots` partial slots slot_stride floats apart (1: p itself).
+// 8 columns per thread, n % 8 == 0.
+__global__ void gated_add_kernel(const float* __restrict__ p, int nslots, int64_t slot_stride,
+                                 const __nv_bfloat16* __restrict__ gate, const __nv_bfloat16* __restrict__ r,
+                                 __nv_bfloat16* __restrict__ out, int base_row, int rows, int n, int length) {
   const int per_row = n / 8;
   const int64_t total = (int64_t)rows * per_row;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int row = (int)(i / per_row), c = (int)(i % per_row) * 8;
     const int64_t off = (int64_t)row * n + c;
-    const float4 p0 = __ldg(reinterpret_cast<const float4*>(p + off));
-    const float4 p1 = __ldg(reinterpret_cast<const float4*>(p + off + 4));
+    float4 p0 = __ldg(reinterpret_cast<const float4*>(p + off));
+    float4 p1 = __ldg(reinterpret_cast<const float4*>(p + off + 4));
+    for (int sl = 1; sl < nslots; ++sl) {
+      const float4 q0 = __ldg(reinterpret_cast<const float4*>(p + sl * slot_stride + off));
+      const float4 q1 = __ldg(reinterpret_cast<const float4*>(p + sl * slot_stride + off + 4));
+      p0 = make_float4(__fadd_rn(p0.x, q0.x), __fadd_rn(p0.y, q0.y), __fadd_rn(p0.z, q0.z), __fadd_rn(p0.w, q0.w));
+      p1 = make_float4(__fadd_rn(p1.x, q1.x), __fadd_rn(p1.y, q1.y), __fadd_rn(p1.z, q1.z), __fadd_rn(p1.w, q1.w));
+    }
     const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(gate + (int64_t)((base_row + row) / length) * n + c));
     const uint4 r4 = __ldg(reinterpret_cast<const uint4*>(r + off));
     const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};

@@ -95,7 +95,8 @@ enum SegKind : int {
   SEG_RESIDUAL = 3,   // bf16(resid + bf16(bf16(p) * gate))
   SEG_SWIGLU = 4,     // SwiGLU of (gate, up) column pairs + H128 + INT4 requant
   SEG_F32 = 5,        // p itself (tests: exact accumulators)
-  SEG_SWIGLU_BF16 = 6 // SwiGLU of (gate, up) column pairs, bf16 h
+  SEG_SWIGLU_BF16 = 6,// SwiGLU of (gate, up) column pairs, bf16 h
+  SEG_F32_SCATTER = 7 // p stored into the owner rank's slot of a peer buffer (tensor-parallel partials)
 };
 
 struct GemmSegment {
@@ -120,6 +121,11 @@ struct GemmParams {
   const float* freqs;              // fp32 [length, 64, 2, 2]
   const __nv_bfloat16* gate;       // SEG_RESIDUAL: bf16 [batch, n]
   const __nv_bfloat16* resid;      // SEG_RESIDUAL: bf16 [M, n]
+  // SEG_F32_SCATTER: row r goes to rank r / scatter_chunk, whose buffer
+  // peer[rank] (fp32 [tp, scatter_chunk, ld], this GPU's or an NVLink peer's)
+  // takes it in slot scatter_rank at row r % scatter_chunk
+  float* peer[4];
+  int scatter_chunk, scatter_rank;
 };
 
 struct WeightMaps {
@@ -477,13 +483,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (ok) {
       const int col0 = n0 + cq * 64;  // first segment column of this thread (non-SwiGLU kinds)
       const bool col_ok = pairw || col0 < S.n;
-      if (S.kind == SEG_F32) {
+      if (S.kind == SEG_F32 || S.kind == SEG_F32_SCATTER) {
         if (row_ok && col_ok) {
-          float* o = reinterpret_cast<float*>(S.out) + (int64_t)row * S.ld + col0;
+          float* o;
+          if (S.kind == SEG_F32) {
+            o = reinterpret_cast<float*>(S.out) + (int64_t)row * S.ld + col0;
+          } else {
+            const int dest = row / p.scatter_chunk;
+            o = p.peer[dest] + ((int64_t)p.scatter_rank * p.scatter_chunk + (row - dest * p.scatter_chunk)) * S.ld +
+                col0;
+          }
 #pragma unroll
           for (int i = 0; i < 64; i += 4)
             *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
         }
+
       } else if (S.kind == SEG_BF16 || S.kind == SEG_SIGMOID) {
         if (row_ok && col_ok) {
           if (S.kind == SEG_SIGMOID) {
@@ -667,6 +681,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // Scatter: the owner rank reads its slots after a stream-ordered barrier
+  // that follows this kernel; one system-scope fence per CTA (cumulative over
+  // the CTA's stores through the barrier above) publishes them.
+  if (p.scatter_chunk > 0 && threadIdx.x == 0) __threadfence_system();
   // The leader's MMAs (which read the peer's shared memory) are complete and
   // no arrival from one CTA to the other is in flight once both get here.
   cluster_sync_all();

@@ -146,7 +146,8 @@ struct SegDesc {
 };
 
 static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDesc* segs, int nseg, int length,
-                       const float* freqs, const void* gate, const void* resid, cudaStream_t st) {
+                       const float* freqs, const void* gate, const void* resid, cudaStream_t st,
+                       void* const* peers = nullptr, int tp = 0, int rank = 0, int chunk = 0) {
   if (M <= 0 || K <= 0 || K % 128 || nseg < 1 || nseg > 4 || length <= 0) return (int)cudaErrorInvalidValue;
   if (!aligned16(a) || !sa) return (int)cudaErrorInvalidValue;
   CUtensorMap amap;
@@ -191,7 +192,8 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     if ((d.kind == SEG_BF16 || d.kind == SEG_SIGMOID || d.kind == SEG_QKNORM || d.kind == SEG_SWIGLU_BF16) &&
         (d.ld % 8 || !aligned16(d.out)))
       return (int)cudaErrorInvalidValue;
-    if (d.kind == SEG_F32 && (d.ld % 4 || !aligned16(d.out))) return (int)cudaErrorInvalidValue;
+    if ((d.kind == SEG_F32 || d.kind == SEG_F32_SCATTER) && (d.ld % 4 || !aligned16(d.out)))
+      return (int)cudaErrorInvalidValue;
     tiles += g.tiles;
   }
   int rc = make_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, (uint64_t)K / 2, (uint64_t)M, (uint64_t)K / 2, 64,
@@ -206,6 +208,18 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
   p.freqs = freqs;
   p.gate = static_cast<const __nv_bfloat16*>(gate);
   p.resid = static_cast<const __nv_bfloat16*>(resid);
+  if (segs[0].kind == SEG_F32_SCATTER) {
+    // rows 0..M-1 go to ranks row / chunk, all of which must exist
+    if (nseg != 1 || !peers || tp < 1 || tp > 4 || rank < 0 || rank >= tp || chunk <= 0 ||
+        (long long)chunk * tp < M)
+      return (int)cudaErrorInvalidValue;
+    for (int i = 0; i < tp; ++i) {
+      if (!aligned16(peers[i])) return (int)cudaErrorInvalidValue;
+      p.peer[i] = static_cast<float*>(peers[i]);
+    }
+    p.scatter_chunk = chunk;
+    p.scatter_rank = rank;
+  }
   const bool pairw = segs[0].kind == SEG_SWIGLU || segs[0].kind == SEG_SWIGLU_BF16;
   void (*kern)(CUtensorMap, WeightMaps, GemmParams) = pairw ? gemm_w4a4_kernel<true> : gemm_w4a4_kernel<false>;
   static bool attr_set[64][2] = {};
@@ -346,20 +360,60 @@ K2B_EXPORT int k2b_norm_mod(const void* x, const void* w, const void* scale, con
                                                (cudaStream_t)stream);
 }
 
-K2B_EXPORT int k2b_gated_add(const void* p, const void* gate, const void* resid, void* out, int base_row, int rows,
-                             int n, int length, void* stream) {
-  if (rows < 0 || n <= 0 || n % 8 || length <= 0 || base_row < 0 || !aligned16(p) || !aligned16(gate) ||
-      !aligned16(resid) || !aligned16(out))
+static int gated_add_launch(const void* p, int nslots, long long slot_stride, const void* gate, const void* resid,
+                            void* out, int base_row, int rows, int n, int length, cudaStream_t st) {
+  if (rows < 0 || n <= 0 || n % 8 || length <= 0 || base_row < 0 || nslots < 1 || nslots > 8 || slot_stride % 4 ||
+      !aligned16(p) || !aligned16(gate) || !aligned16(resid) || !aligned16(out))
     return (int)cudaErrorInvalidValue;
   if (rows == 0) return 0;
   const long long work = (long long)rows * (n / 8);
   const long long blocks = (work + 255) / 256;
   const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
-  gated_add_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const float*>(p), static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(resid),
-      static_cast<__nv_bfloat16*>(out), base_row, rows, n, length);
+  gated_add_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(p), nslots, (int64_t)slot_stride,
+                                         static_cast<const __nv_bfloat16*>(gate),
+                                         static_cast<const __nv_bfloat16*>(resid), static_cast<__nv_bfloat16*>(out),
+                                         base_row, rows, n, length);
   return launch_status();
 }
+
+K2B_EXPORT int k2b_gated_add(const void* p, const void* gate, const void* resid, void* out, int base_row, int rows,
+                             int n, int length, void* stream) {
+  return gated_add_launch(p, 1, 0, gate, resid, out, base_row, rows, n, length, (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_reduce_gated_add(const void* slots, int nslots, long long slot_stride, const void* gate,
+                                    const void* resid, void* out, int base_row, int rows, int n, int length,
+                                    void* stream) {
+  return gated_add_launch(slots, nslots, slot_stride, gate, resid, out, base_row, rows, n, length,
+                          (cudaStream_t)stream);
+}
+
+// --------------------------------------------- peer buffers (CUDA IPC)
+// A device buffer another process on this node can map: the tensor-parallel
+// receive slots of k2b_gemm_f32_scatter.  handle: 64 bytes (cudaIpcMemHandle_t).
+K2B_EXPORT int k2b_ipc_alloc(long long bytes, void** ptr, void* handle) {
+  if (bytes <= 0 || !ptr || !handle) return (int)cudaErrorInvalidValue;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return (int)e;
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return (int)e;
+  }
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return 0;
+}
+K2B_EXPORT int k2b_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return (int)cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+K2B_EXPORT int k2b_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
+K2B_EXPORT int k2b_ipc_free(void* ptr) { return (int)cudaFree(ptr); }
 
 K2B_EXPORT int k2b_elementwise(const void* a, const void* b, const void* r, void* y, long long n, int mode, int width,
                                void* stream) {
@@ -405,6 +459,19 @@ K2B_EXPORT int k2b_gemm_f32(const void* a, const void* sa, const void* w, const 
                             int k, void* stream) {
   SegDesc d = {SEG_F32, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
   return gemm_launch(a, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+// fp32 a@W of a tensor-parallel rank, stored straight into the owners' receive
+// buffers: row r goes to peers[r / chunk] (fp32 [tp, chunk, n], local or an
+// NVLink peer's mapping) in slot `rank`, row r % chunk.  The owner sums its tp
+// slots (k2b_reduce_gated_add) after a barrier that follows this launch on
+// every rank.
+K2B_EXPORT int k2b_gemm_f32_scatter(const void* a, const void* sa, const void* w, const void* wscale,
+                                    void* const* peers, int tp, int rank, int chunk, int m, int n, int k,
+                                    void* stream) {
+  if (!peers) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_F32_SCATTER, n, w, wscale, peers[0], n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, peers, tp, rank, chunk);
 }
 
 K2B_EXPORT int k2b_gemm_bf16(const void* a, const void* sa, const void* w, const void* wscale, void* out, int m, int n,

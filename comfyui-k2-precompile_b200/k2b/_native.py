@@ -28,6 +28,12 @@ SIGNATURES = {
     "k2b_qkv": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
     "k2b_gated_residual": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
     "k2b_gated_add": (_I, [_P] * 4 + [_I, _I, _I, _I, _P]),
+    "k2b_reduce_gated_add": (_I, [_P, _I, ctypes.c_longlong, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "k2b_gemm_f32_scatter": (_I, [_P] * 5 + [_I] * 6 + [_P]),
+    "k2b_ipc_alloc": (_I, [ctypes.c_longlong, _P, _P]),
+    "k2b_ipc_open": (_I, [_P, _P]),
+    "k2b_ipc_close": (_I, [_P]),
+    "k2b_ipc_free": (_I, [_P]),
     "k2b_norm_quant_rows": (_I, [_P] * 6 + [_I, _I, _I, _I, _I, _I, _F, _P]),
     "k2b_swiglu_quant": (_I, [_P] * 8 + [_I, _I, _I, _P]),
     "k2b_swiglu_bf16": (_I, [_P] * 7 + [_I, _I, _I, _P]),

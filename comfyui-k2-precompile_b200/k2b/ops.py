@@ -157,6 +157,22 @@ def gated_add(p: torch.Tensor, gate: torch.Tensor, residual: torch.Tensor, *, ba
     return out
 
 
+def reduce_gated_add(slots_ptr: int, nslots: int, slot_stride: int, gate: torch.Tensor, residual: torch.Tensor, *,
+                     base_row: int, length: int, out: torch.Tensor) -> torch.Tensor:
+    """out = gated_add of p = ((s_0 + s_1) + ...) over ``nslots`` fp32 slots
+    of a receive buffer (``slots_ptr``: this rank's first row in slot 0,
+    ``slot_stride`` floats between slots), k2b_reduce_gated_add."""
+    _cuda(gate, residual, out)
+    _need(gate.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16 and out.dtype == torch.bfloat16,
+          "reduce_gated_add: bf16 gate/residual/out expected")
+    n = int(residual.shape[-1])
+    rows = residual.numel() // n
+    _need(out.numel() == rows * n and gate.shape[-1] == n and 1 <= nslots <= 8, "reduce_gated_add: shapes")
+    check(lib().k2b_reduce_gated_add(ctypes.c_void_p(slots_ptr), nslots, slot_stride, _p(gate), _p(residual), _p(out),
+                                     base_row, rows, n, length, _stream()), "k2b_reduce_gated_add")
+    return out
+
+
 def norm_mod(x: torch.Tensor, w: torch.Tensor, scale: Optional[torch.Tensor] = None,
              shift: Optional[torch.Tensor] = None, *, length: Optional[int] = None, cut: int = -1,
              eps: float = 1e-6) -> torch.Tensor:
@@ -244,6 +260,19 @@ def gemm_f32(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, out: Optional
     check(lib().k2b_gemm_f32(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
           "k2b_gemm_f32")
     return out
+
+
+def gemm_f32_scatter(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, peers, rank: int, chunk: int) -> None:
+    """fp32 a@W written into the owners' receive buffers (k2b_gemm_f32_scatter):
+    row r to ``peers[r // chunk]`` (device pointers, fp32 [tp, chunk, n] each)
+    in slot ``rank``."""
+    _cuda(a, sa, W.w, W.scale)
+    m = _act(a, sa, W.k)
+    tp = len(peers)
+    _need(1 <= tp <= 4 and 0 <= rank < tp and chunk > 0 and chunk * tp >= m, "gemm_f32_scatter: rank layout")
+    arr = (ctypes.c_void_p * tp)(*[int(x) for x in peers])
+    check(lib().k2b_gemm_f32_scatter(_p(a), _p(sa), _p(W.w), _p(W.scale), arr, tp, rank, chunk, m, W.n, W.k,
+                                     _stream()), "k2b_gemm_f32_scatter")
 
 
 def gemm_bf16(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Tensor:
@@ -370,7 +399,7 @@ def device_error(reset: bool = True) -> int:
 
 
 __all__ = [
-    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_quant_rows", "gated_add", "norm_mod", "elementwise", "rope", "rotate_quant",
-    "gemm_f32", "gemm_bf16", "qkv",
+    "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_quant_rows", "gated_add", "reduce_gated_add", "norm_mod", "elementwise", "rope", "rotate_quant",
+    "gemm_f32", "gemm_f32_scatter", "gemm_bf16", "qkv",
     "gated_residual", "swiglu_quant", "swiglu_bf16", "attention", "attention_quant", "device_error",
 ]

@@ -25,6 +25,13 @@ group's batch*length rows, c = ceil(rows/tp).  One block:
   6. down-projection over own K-slice, fp32 partial    -> reduce-scatter (sum)
   7. gated residual of own rows.
 
+With ``fused=True`` the reduce-scatter half is done by the projection
+itself: its epilogue stores each fp32 partial tile straight into the owner
+rank's receive buffer over NVLink (CUDA-IPC mapped peer memory,
+k2b_gemm_f32_scatter), so the transfer overlaps the GEMM tile by tile; a
+stream-ordered barrier (a one-element NCCL all-reduce) follows, and the owner
+sums its slots inside the gated-residual kernel (k2b_reduce_gated_add).
+
 Steps 3-4 and 6-7 are the all-reduce after the out- and down-projections,
 split into its reduce-scatter and all-gather halves around the row-local work
 between them, so the gated residual and norm_quant run once per row rather
@@ -209,6 +216,60 @@ PHASES = ["norm_quant_pre", "gather_act", "qkv_qknorm_rope", "attention_quant", 
           "down_proj_partial", "reduce_scatter_down", "gated_add"]
 
 
+class PeerSlots:
+    """Receive buffers of one tensor-parallel group for the fused scatter:
+    ``ptrs[j]`` is rank j's buffer (fp32 [tp, chunk, n]) as this process sees
+    it, ``ptrs[rank]`` its own."""
+
+    def __init__(self, ptrs: Sequence[int], rank: int, owned=None, mapped=()):
+        self.ptrs, self.rank = [int(x) for x in ptrs], rank
+        self._owned, self._mapped = owned, list(mapped)
+
+    @classmethod
+    def ipc(cls, nbytes: int, rank: int, tp: int, group) -> "PeerSlots":
+        """Collective over ``group``: every rank allocates its buffer with
+        k2b_ipc_alloc and maps the others' through CUDA IPC."""
+        import ctypes
+
+        import torch.distributed as dist
+
+        from ._native import check, lib
+
+        L = lib()
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        check(L.k2b_ipc_alloc(nbytes, ctypes.byref(own), handle), "k2b_ipc_alloc")
+        handles = [None] * tp
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs, mapped = [], []
+        for j, h in enumerate(handles):
+            if j == rank:
+                ptrs.append(own.value)
+                continue
+            peer = ctypes.c_void_p()
+            buf = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            check(L.k2b_ipc_open(buf, ctypes.byref(peer)), "k2b_ipc_open")
+            ptrs.append(peer.value)
+            mapped.append(peer.value)
+        return cls(ptrs, rank, owned=own.value, mapped=mapped)
+
+    def close(self) -> None:
+        """Unmap the peers and free the own buffer (call after every rank has
+        finished using them)."""
+        if self._owned is None and not self._mapped:
+            return
+        import ctypes
+
+        from ._native import lib
+
+        L = lib()
+        for ptr in self._mapped:
+            L.k2b_ipc_close(ctypes.c_void_p(ptr))
+        if self._owned is not None:
+            L.k2b_ipc_free(ctypes.c_void_p(self._owned))
+        self._owned, self._mapped = None, []
+
+
 class TPBlocks:
     """One rank's share of a KV-head tensor-parallel block stack.
 
@@ -217,7 +278,7 @@ class TPBlocks:
     form the group's row space, of which this rank holds ``self.shard``."""
 
     def __init__(self, cfg: ModelConfig, blocks: List[BlockWeights], plan: TPPlan, group, batch: int, length: int,
-                 device="cuda"):
+                 device="cuda", fused: bool = False):
         self.cfg, self.blocks, self.plan, self.group = cfg, blocks, plan, group
         self.batch, self.length = batch, length
         rows = batch * length
@@ -231,10 +292,34 @@ class TPBlocks:
         dev = torch.device(device)
         self.act_q = torch.zeros((pad, H // 2), dtype=torch.uint8, device=dev)
         self.act_s = torch.zeros((pad, H // GROUP), dtype=torch.float16, device=dev)
-        self.partial = torch.zeros((pad, H), dtype=torch.float32, device=dev)  # pad rows stay zero
-        self.reduced = torch.empty((c, H), dtype=torch.float32, device=dev)
+        if not fused:  # NCCL reduce-scatter buffers (pad rows stay zero)
+            self.partial = torch.zeros((pad, H), dtype=torch.float32, device=dev)
+            self.reduced = torch.empty((c, H), dtype=torch.float32, device=dev)
         self.x1 = torch.empty((c, H), dtype=torch.bfloat16, device=dev)
         self.hq_heads, self.kv_heads_local, self.f_local = hq, kvh, f
+        # fused reduce-scatter: receive slots fp32 [tp, chunk, hidden] per rank
+        self.fused = fused
+        self.slot_bytes = tp * c * H * 4
+        self.peers: Optional[PeerSlots] = None
+        if fused and group is not None and tp > 1:
+            self.peers = PeerSlots.ipc(self.slot_bytes, plan.rank, tp, group)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def attach_peers(self, peers: PeerSlots) -> None:
+        """Receive buffers set up by the caller (one process driving all ranks)."""
+        self.peers = peers
+
+    def close(self) -> None:
+        """Release the receive buffers (collective when they are IPC-mapped:
+        every rank waits until all have stopped writing into them)."""
+        if self.peers is not None:
+            if self.peers._mapped or self.peers._owned is not None:
+                import torch.distributed as dist
+
+                torch.cuda.synchronize()
+                dist.barrier(group=self.group)
+            self.peers.close()
+            self.peers = None
 
     def _steps(self, x: torch.Tensor, freqs: torch.Tensor, events=None) -> Iterator[tuple]:
         """The block loop with its collectives as yielded requests:
@@ -263,12 +348,21 @@ class TPBlocks:
             oq, os_ = ops.attention_quant(qv, kv, vv)
             del q, k, v, qv, kv, vv
             mark(e + 4)
-            ops.gemm_f32(oq, os_, blk.wo, out=self.partial[:rows])
-            del oq, os_
-            mark(e + 5)
-            yield ("reduce_scatter", self.reduced, self.partial)
-            mark(e + 6)
-            ops.gated_add(self.reduced[:n], pg, x[:n], base_row=base, length=L, out=self.x1[:n])
+            if self.fused:
+                ops.gemm_f32_scatter(oq, os_, blk.wo, self.peers.ptrs, r, c)
+                del oq, os_
+                mark(e + 5)
+                yield ("barrier",)
+                mark(e + 6)
+                ops.reduce_gated_add(self.peers.ptrs[r], self.plan.tp, c * cfg.hidden, pg, x[:n], base_row=base,
+                                     length=L, out=self.x1[:n])
+            else:
+                ops.gemm_f32(oq, os_, blk.wo, out=self.partial[:rows])
+                del oq, os_
+                mark(e + 5)
+                yield ("reduce_scatter", self.reduced, self.partial)
+                mark(e + 6)
+                ops.gated_add(self.reduced[:n], pg, x[:n], base_row=base, length=L, out=self.x1[:n])
             ops.norm_quant_rows(self.x1[:n], blk.postnorm, ss, shf, base_row=base, length=L, batch=B, eps=cfg.eps,
                                 out=(self.act_q[slot], self.act_s[slot]))
             mark(e + 7)
@@ -276,12 +370,21 @@ class TPBlocks:
             mark(e + 8)
             hq, hs = ops.swiglu_quant(self.act_q[:rows], self.act_s[:rows], blk.wg, blk.wu)
             mark(e + 9)
-            ops.gemm_f32(hq, hs, blk.wd, out=self.partial[:rows])
-            del hq, hs
-            mark(e + 10)
-            yield ("reduce_scatter", self.reduced, self.partial)
-            mark(e + 11)
-            ops.gated_add(self.reduced[:n], sg, self.x1[:n], base_row=base, length=L, out=x[:n])
+            if self.fused:
+                ops.gemm_f32_scatter(hq, hs, blk.wd, self.peers.ptrs, r, c)
+                del hq, hs
+                mark(e + 10)
+                yield ("barrier",)
+                mark(e + 11)
+                ops.reduce_gated_add(self.peers.ptrs[r], self.plan.tp, c * cfg.hidden, sg, self.x1[:n],
+                                     base_row=base, length=L, out=x[:n])
+            else:
+                ops.gemm_f32(hq, hs, blk.wd, out=self.partial[:rows])
+                del hq, hs
+                mark(e + 10)
+                yield ("reduce_scatter", self.reduced, self.partial)
+                mark(e + 11)
+                ops.gated_add(self.reduced[:n], sg, self.x1[:n], base_row=base, length=L, out=x[:n])
             if events is not None:
                 e += len(PHASES)
         if events is not None:
@@ -295,6 +398,14 @@ class TPBlocks:
         self._check(x, freqs, events)
         tp, c = self.plan.tp, self.shard.chunk
         for req in self._steps(x, freqs, events):
+            if req[0] == "barrier":
+                # stream-ordered: every rank's scatter GEMM has finished before
+                # any rank's reduce reads its slots
+                if tp > 1:
+                    import torch.distributed as dist
+
+                    dist.all_reduce(self._flag, group=self.group)
+                continue
             if tp == 1:
                 if req[0] == "reduce_scatter":
                     req[1].copy_(req[2][:c])
@@ -312,8 +423,19 @@ class TPBlocks:
                   "tensor-parallel forward: x must be this rank's [chunk, hidden] bf16 rows")
         ops._need(freqs.dtype == torch.float32 and freqs.numel() == self.length * 256,
                   "tensor-parallel forward: freqs shape")
+        ops._need(not self.fused or self.peers is not None, "fused tensor-parallel forward: receive buffers not set")
         if events is not None:
             ops._need(len(events) == len(PHASES) * len(self.blocks) + 1, "tensor-parallel forward: event count")
+
+
+def local_peer_slots(ranks: Sequence[TPBlocks]) -> List[torch.Tensor]:
+    """Receive buffers for fused ranks driven by one process on one device
+    (run_lockstep): every rank sees every buffer directly."""
+    bufs = [torch.empty(m.slot_bytes // 4, dtype=torch.float32, device=m._flag.device) for m in ranks]
+    ptrs = [b.data_ptr() for b in bufs]
+    for m in ranks:
+        m.attach_peers(PeerSlots(ptrs, m.plan.rank))
+    return bufs
 
 
 def run_lockstep(ranks: Sequence[TPBlocks], xs: Sequence[torch.Tensor], freqs: torch.Tensor) -> None:
@@ -331,6 +453,8 @@ def run_lockstep(ranks: Sequence[TPBlocks], xs: Sequence[torch.Tensor], freqs: t
             return
         if any(r is None or r[0] != reqs[0][0] for r in reqs):
             raise RuntimeError("tensor-parallel ranks diverged")
+        if reqs[0][0] == "barrier":  # one stream: the scatter kernels already ran
+            continue
         if reqs[0][0] == "gather":
             for j, rj in enumerate(reqs):
                 for bi in range(len(rj[1])):

@@ -135,6 +135,30 @@ int k2b_gated_residual(const void* a, const void* sa, const void* w, const void*
 int k2b_gated_add(const void* p, const void* gate, const void* resid, void* out, int base_row, int rows, int n,
                   int length, void* stream);
 
+/* fp32 a@W of one tensor-parallel rank written straight into the owners'
+ * receive buffers over NVLink peer memory (the GEMM half of a fused
+ * reduce-scatter): row r goes to peers[r/chunk] (fp32 [tp, chunk, n], this
+ * GPU's buffer or a peer's CUDA-IPC mapping, tp <= 4) in slot `rank` at row
+ * r%chunk, so the transfer overlaps the math tile by tile.  The owner sums
+ * its slots with k2b_reduce_gated_add after a barrier that follows this
+ * launch on every rank.  Replaces the NCCL reduce-scatter of the fp32
+ * partials after the out- and down-projections. */
+int k2b_gemm_f32_scatter(const void* a, const void* sa, const void* w, const void* wscale, void* const* peers, int tp,
+                         int rank, int chunk, int m, int n, int k, void* stream);
+
+/* k2b_gated_add of p = ((s_0 + s_1) + ...) + s_{nslots-1}, the fp32 sum of
+ * nslots partial slots slot_stride floats apart (the receive buffer of
+ * k2b_gemm_f32_scatter, base at this rank's first row). */
+int k2b_reduce_gated_add(const void* slots, int nslots, long long slot_stride, const void* gate, const void* resid,
+                         void* out, int base_row, int rows, int n, int length, void* stream);
+
+/* Peer buffers for the scatter: cudaMalloc + IPC handle (64 bytes), open /
+ * close a peer's handle in another process, free. */
+int k2b_ipc_alloc(long long bytes, void** ptr, void* handle);
+int k2b_ipc_open(const void* handle, void** ptr);
+int k2b_ipc_close(void* ptr);
+int k2b_ipc_free(void* ptr);
+
 /* Gate/up projection + SwiGLU + INT4 requant of the down-projection input:
  * h = bf16(bf16(silu(bf16(pg)))*bf16(pu)), then H128 rotation + group-128
  * INT4 -> hq u8 [m, width/2], hs fp16 [m, width/128].  Replaces

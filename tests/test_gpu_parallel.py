@@ -87,16 +87,89 @@ def test_qkv_kv_shard_of_three_heads(cuda):
     assert np.array_equal(bits(v), O.bf16_bits(O.gemm_w4a4(a, sa, *ws["v"])))
 
 
-def _tp_models(cuda, cfg, tp, batch, length, seed=3):
+def test_gemm_f32_scatter_places_rows_in_owner_slots(cuda):
+    import torch
+    from k2b import ops
+
+    M, N, K, tp, rank = 300, 384, 512, 3, 1
+    chunk = -(-M // tp)
+    a, sa = packed_act(M, K, 21)
+    w, sw = packed_weight(N, K, 22)
+    W = ops.prepare_weight(t_u8(w, cuda), t_f16(sw, cuda))
+    bufs = [torch.full((tp, chunk, N), float("nan"), device=cuda) for _ in range(tp)]
+    ops.gemm_f32_scatter(t_u8(a, cuda), t_f16(sa, cuda), W, [b.data_ptr() for b in bufs], rank, chunk)
+    torch.cuda.synchronize()
+    ref = O.gemm_w4a4(a, sa, w, sw)
+    for dest in range(tp):
+        lo, hi = dest * chunk, min(M, (dest + 1) * chunk)
+        got = bufs[dest][rank, :hi - lo].cpu().numpy()
+        assert np.array_equal(got, ref[lo:hi]), dest
+        for other in range(tp):  # only slot `rank` is written
+            if other != rank:
+                assert torch.isnan(bufs[dest][other]).all()
+
+
+def test_reduce_gated_add_sums_slots_in_order(cuda):
+    import torch
+    from k2b import ops
+
+    tp, chunk, n, rows, base, length = 3, 40, 256, 37, 80, 50
+    rng = np.random.default_rng(8)
+    slots = (rng.standard_normal((tp, chunk, n)) * 3).astype(np.float32)
+    gate = O.bf16_bits(rng.normal(0, 0.1, (4, n)).astype(np.float32))
+    resid = O.bf16_bits(rng.standard_normal((rows, n)).astype(np.float32))
+    sl = t_f32(slots, cuda)
+    out = torch.empty((rows, n), dtype=torch.bfloat16, device=cuda)
+    ops.reduce_gated_add(sl.data_ptr(), tp, chunk * n, t_bf16(gate, cuda), t_bf16(resid, cuda), base_row=base,
+                         length=length, out=out)
+    torch.cuda.synchronize()
+    p = slots[0, :rows].copy()
+    for s_ in range(1, tp):
+        p = (p + slots[s_, :rows]).astype(np.float32)  # fp32, slot order
+    idx = (base + np.arange(rows)) // length
+    assert np.array_equal(bits(out), O.gated_residual(p, gate[idx], resid, 1))
+
+
+def _tp_models(cuda, cfg, tp, batch, length, seed=3, fused=False):
     from k2b.model import synthetic_blocks
-    from k2b.parallel import TPBlocks, TPPlan, shard_fn
+    from k2b.parallel import TPBlocks, TPPlan, local_peer_slots, shard_fn
 
     ranks = []
     for r in range(tp):
         plan = TPPlan.of(cfg, tp, r)
         bw = synthetic_blocks(cfg, batch, seed=seed, device=cuda, shard=shard_fn(plan))
-        ranks.append(TPBlocks(cfg, bw, plan, None, batch, length, device=cuda))
+        ranks.append(TPBlocks(cfg, bw, plan, None, batch, length, device=cuda, fused=fused))
+    if fused:
+        ranks[0]._slot_bufs = local_peer_slots(ranks)  # keep the buffers alive with the ranks
     return ranks
+
+
+@pytest.mark.parametrize("tp,batch,length", [(2, 2, 150), (4, 1, 203)])
+def test_tp_lockstep_fused_scatter_equals_reduce_scatter(cuda, tp, batch, length):
+    """The fused scatter path sums the same fp32 partials in the same rank
+    order as the reduce-scatter emulation: bit-identical block outputs."""
+    import torch
+    from k2b.model import ModelConfig, rope_positions, rope_table
+    from k2b.parallel import run_lockstep
+
+    cfg = ModelConfig(hidden=1024, heads=8, kvheads=4, mlp=2048, blocks=2)
+    side = 12
+    freqs = rope_table(rope_positions(length - (length // side) * side, length // side, side), (64, 64)).to(cuda)
+    rng = np.random.default_rng(9)
+    xb = O.bf16_bits(rng.standard_normal((batch * length, cfg.hidden)).astype(np.float32))
+    outs = []
+    for fused in (False, True):
+        ranks = _tp_models(cuda, cfg, tp, batch, length, fused=fused)
+        xs = []
+        for m in ranks:
+            sh = m.shard
+            xr = torch.zeros((sh.chunk, cfg.hidden), dtype=torch.bfloat16, device=cuda)
+            xr[:sh.count] = t_bf16(xb[sh.base:sh.base + sh.count], cuda)
+            xs.append(xr)
+        run_lockstep(ranks, xs, freqs)
+        torch.cuda.synchronize()
+        outs.append(torch.cat([x[:m.shard.count] for m, x in zip(ranks, xs)], 0))
+    assert torch.equal(outs[0], outs[1])
 
 
 @pytest.mark.parametrize("tp,batch,length", [(2, 2, 150), (4, 1, 203)])
@@ -129,7 +202,7 @@ def test_tp_lockstep_matches_native_block_loop(cuda, tp, batch, length):
     assert (g == r).mean() >= 0.98  # fp32 reassociation of projection sums only
 
 
-def _nccl_rank(rank, world, port, path):
+def _nccl_rank(rank, world, port, path, fused=False):
     import datetime
 
     import torch
@@ -148,7 +221,7 @@ def _nccl_rank(rank, world, port, path):
         topo = topology(world, rank, world)
         plan = TPPlan.of(cfg, world, rank)
         bw = synthetic_blocks(cfg, batch, seed=3, device=dev, shard=shard_fn(plan))
-        m = TPBlocks(cfg, bw, plan, topo.tp_group, batch, length, device=dev)
+        m = TPBlocks(cfg, bw, plan, topo.tp_group, batch, length, device=dev, fused=fused)
         freqs = rope_table(rope_positions(6, 12, 12), (64, 64)).to(dev)
         rng = np.random.default_rng(4)
         xb = O.bf16_bits(rng.standard_normal((batch * length, cfg.hidden)).astype(np.float32))
@@ -158,12 +231,14 @@ def _nccl_rank(rank, world, port, path):
         m.forward_(x, freqs)
         torch.cuda.synchronize()
         np.save(f"{path}.{rank}.npy", bits(x[:sh.count]))
+        m.close()
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
 
 
-def test_tp2_nccl_matches_native_block_loop(cuda, tmp_path):
+@pytest.mark.parametrize("fused", [False, True])
+def test_tp2_nccl_matches_native_block_loop(cuda, tmp_path, fused):
     import socket
 
     import torch
@@ -176,7 +251,7 @@ def test_tp2_nccl_matches_native_block_loop(cuda, tmp_path):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     path = str(tmp_path / "tp")
-    mp.start_processes(_nccl_rank, args=(2, port, path), nprocs=2, start_method="spawn")
+    mp.start_processes(_nccl_rank, args=(2, port, path, fused), nprocs=2, start_method="spawn")
     got = np.concatenate([np.load(f"{path}.{r}.npy") for r in range(2)], 0)
     cfg = ModelConfig(hidden=1024, heads=8, kvheads=4, mlp=2048, blocks=2)
     batch, length = 2, 150
