@@ -99,6 +99,13 @@ def cpu_sample_latent_seconds(rows_sample: int = 8, seed: int = 0):
     return per_latent, O._workers(), note
 
 
+def workload_config():
+    """The config-4 workload keys shared by both bench arms."""
+    return {"workload": "config 4: 8 latents x 4224 tokens (128 text + 64x64 image), 28 Krea2 blocks",
+            "latents": LATENTS, "tokens_per_latent": LENGTH, "blocks": 28, "hidden": 6144, "heads": 48,
+            "kvheads": 12, "mlp": 16384}
+
+
 def run_reference(args, rank):
     """--impl reference: the reference path's CPU restatement (the reference's
     own kernels are SM89 CUDA + un-vendored comfy-kitchen and cannot build
@@ -116,10 +123,10 @@ def run_reference(args, rank):
     line = {
         "metric": METRIC, "value": value, "unit": "latents/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_latent * LATENTS * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "w4a4-int/bf16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "w4a4-s8xs8->s32 / bf16 attention",
         "data": "synthetic",
-        "config": {"workload": "config 4: 8 latents x 4224 tokens, 28 blocks (CPU: sampled rows, extrapolated)",
-                   "latents": LATENTS, "tokens": LENGTH, "blocks": 28, "parallelism": "cpu"},
+        "config": dict(workload_config(), parallelism=f"host CPU, {threads} threads",
+                       sampling="bounded row sample per step, extrapolated (see cpu_baseline.sample)"),
         "cpu_baseline": {"value": value, "unit": "latents/s", "cores": threads, "kind": "port", "sample": note},
         "e2e": {"value": value, "unit": "latents/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -630,11 +637,9 @@ def main():
             "metric": METRIC, "value": value, "unit": "latents/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "w4a4-s8xs8->s32 / bf16 attention", "data": "synthetic",
-            "config": {"workload": "config 4: 8 latents x 4224 tokens (128 text + 64x64 image), 28 Krea2 blocks",
-                       "latents": LATENTS, "tokens_per_latent": LENGTH, "blocks": cfg.blocks,
-                       "hidden": cfg.hidden, "heads": cfg.heads, "kvheads": cfg.kvheads, "mlp": cfg.mlp,
-                       "parallelism": par, "tp": tp, "dp": topo.dp, "latents_per_group": local,
-                       "l2": "inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"},
+            "config": dict(workload_config(),
+                       parallelism=par, tp=tp, dp=topo.dp, latents_per_group=local,
+                       l2="inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"),
             "forward_ms_4050": fwd4050,
             "e2e": {"value": e2e_value, "unit": "latents/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": x_host.numel() * 2 * world,

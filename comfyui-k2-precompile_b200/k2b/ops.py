@@ -95,7 +95,7 @@ def norm_quant(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: tor
     K = int(x.shape[-1])
     rows = x.numel() // K
     if length is None:
-        length = int(x.shape[-2]) if x.dim() == 3 else rows
+        length = (int(x.shape[-2]) if x.dim() == 3 else rows) or 1
     batch = max(1, rows // length)
     _need(w.numel() == K and scale.shape[-1] == K and shift.shape[-1] == K, "norm_quant: width mismatch")
     nb = scale.numel() // K
@@ -103,6 +103,8 @@ def norm_quant(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: tor
           "norm_quant: modulation rows do not cover the batch")
     q = torch.empty((rows, K // 2), dtype=torch.uint8, device=x.device)
     s = torch.empty((rows, K // GROUP), dtype=torch.float16, device=x.device)
+    if rows == 0:  # empty batch: empty outputs, no launch
+        return q, s
     check(lib().k2b_norm_quant(_p(x), _p(w), _p(scale), _p(shift), _p(q), _p(s), rows, K, length, cut, batch,
                                ctypes.c_float(eps), _stream()), "k2b_norm_quant")
     return q, s
@@ -186,13 +188,15 @@ def norm_mod(x: torch.Tensor, w: torch.Tensor, scale: Optional[torch.Tensor] = N
     rows = x.numel() // K
     _need(w.numel() == K, "norm_mod: width mismatch")
     if length is None:
-        length = int(x.shape[-2]) if x.dim() == 3 else rows
+        length = (int(x.shape[-2]) if x.dim() == 3 else rows) or 1
     batch = max(1, rows // length)
     if scale is not None:
         _need(scale.dtype == torch.bfloat16 and shift.dtype == torch.bfloat16 and scale.shape[-1] == K and
               shift.numel() == scale.numel(), "norm_mod: bf16 modulation [nb, K] expected")
         _need(scale.numel() // K >= (2 * batch if cut >= 0 else batch), "norm_mod: modulation rows do not cover the batch")
     y = torch.empty_like(x)
+    if rows == 0:
+        return y
     check(lib().k2b_norm_mod(_p(x), _p(w), _p(scale), _p(shift), _p(y), rows, K, length, cut, batch,
                              ctypes.c_float(eps), _stream()), "k2b_norm_mod")
     return y
@@ -235,6 +239,8 @@ def rotate_quant(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     rows = x.numel() // K
     q = torch.empty((rows, K // 2), dtype=torch.uint8, device=x.device)
     s = torch.empty((rows, K // GROUP), dtype=torch.float16, device=x.device)
+    if rows == 0:
+        return q, s
     check(lib().k2b_rotate_quant(_p(x), _p(q), _p(s), rows, K, _stream()), "k2b_rotate_quant")
     return q, s
 
@@ -257,6 +263,8 @@ def gemm_f32(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, out: Optional
     if out is None:
         out = torch.empty((m, W.n), dtype=torch.float32, device=a.device)
     _need(out.dtype == torch.float32 and out.dim() == 2 and tuple(out.shape) == (m, W.n), "gemm_f32: out shape")
+    if m == 0:
+        return out
     check(lib().k2b_gemm_f32(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
           "k2b_gemm_f32")
     return out
@@ -279,6 +287,8 @@ def gemm_bf16(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Ten
     _cuda(a, sa, W.w, W.scale)
     m = _act(a, sa, W.k)
     out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
+    if m == 0:
+        return out
     check(lib().k2b_gemm_bf16(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
           "k2b_gemm_bf16")
     return out
@@ -305,6 +315,8 @@ def qkv(a: torch.Tensor, sa: torch.Tensor, wq: PreparedWeight, wk: PreparedWeigh
     if wg is not None:
         _need(wg.n == wq.n and wg.k == wq.k, "qkv gate weight shape")
         go = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
+    if m == 0:
+        return qo, ko, vo, go
     check(lib().k2b_qkv(_p(a), _p(sa), _p(wq.w), _p(wq.scale), _p(wk.w), _p(wk.scale), _p(wv.w), _p(wv.scale),
                         _p(None if wg is None else wg.w), _p(None if wg is None else wg.scale), _p(nq), _p(nk),
                         _p(freqs), _p(qo), _p(ko), _p(vo), _p(go), m, length, wq.n, wk.n, wq.k,
@@ -321,6 +333,8 @@ def gated_residual(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, gate: t
     _need(residual.numel() == m * W.n and gate.numel() == (m // length) * W.n and m % length == 0,
           "gated_residual: shapes")
     out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
+    if m == 0:
+        return out
     check(lib().k2b_gated_residual(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(gate), _p(residual), _p(out), m, length,
                                    W.n, W.k, _stream()), "k2b_gated_residual")
     return out
@@ -334,6 +348,8 @@ def swiglu_quant(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: Prep
     F = wg.n
     hq = torch.empty((m, F // 2), dtype=torch.uint8, device=a.device)
     hs = torch.empty((m, F // GROUP), dtype=torch.float16, device=a.device)
+    if m == 0:
+        return hq, hs
     check(lib().k2b_swiglu_quant(_p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(hq), _p(hs), m,
                                  F, wg.k, _stream()), "k2b_swiglu_quant")
     return hq, hs
@@ -344,6 +360,8 @@ def swiglu_bf16(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: Prepa
     m = _act(a, sa, wg.k)
     _need(wu.n == wg.n and wu.k == wg.k, "swiglu weight shapes")
     h = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
+    if m == 0:
+        return h
     check(lib().k2b_swiglu_bf16(_p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(h), m, wg.n,
                                 wg.k, _stream()), "k2b_swiglu_bf16")
     return h
@@ -389,6 +407,8 @@ def attention_quant(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     _need(k.shape[0] == B and k.shape[:3] == v.shape[:3] and H % k.shape[1] == 0, "attention: GQA shapes")
     oq = torch.empty((B * L, H * D // 2), dtype=torch.uint8, device=q.device)
     os_ = torch.empty((B * L, H), dtype=torch.float16, device=q.device)
+    if B * L == 0:
+        return oq, os_
     check(lib().k2b_attention_quant(_p(q), _p(k), _p(v), _p(oq), _p(os_), B, H, int(k.shape[1]), L,
                                     int(k.shape[2]), D, *qs, *ks, *vs, _stream()), "k2b_attention_quant")
     return oq, os_
