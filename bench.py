@@ -412,10 +412,10 @@ def main():
     ap.add_argument("--tp", type=int, default=1,
                     help="KV-head tensor-parallel degree (1, 2, 4); the remaining factor of the world is batch "
                          "sharding (8 GPUs: --tp 4 gives 4-way head TP x 2-way batch)")
-    ap.add_argument("--tp-fused", action="store_true",
-                    help="with --tp: the out/down projections store their fp32 partials straight into the owner "
-                         "rank's buffer over NVLink peer memory (k2b_gemm_f32_scatter) instead of an NCCL "
-                         "reduce-scatter after them")
+    ap.add_argument("--tp-nccl", action="store_true",
+                    help="with --tp: an NCCL reduce-scatter of the fp32 partials after the out/down projections "
+                         "instead of the default fused projection that stores them straight into the owner rank's "
+                         "buffer over NVLink peer memory (k2b_gemm_f32_scatter)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="profile mode: norm_quant|qkv|out_proj|gate_up|down|attention on one small case")
@@ -462,7 +462,7 @@ def main():
     peaks, peak_kind = measured_peaks()
     int8_tops = int8_peak_tops(torch) if rank == 0 else None
 
-    wl = Workload(torch, cfg, topo, dev, local, fused=args.tp_fused)
+    wl = Workload(torch, cfg, topo, dev, local, fused=not args.tp_nccl)
     freqs = wl.freqs
     rows = wl.rows_here
     # this rank's hidden-state rows of its group's latents (whole latents when tp == 1)
@@ -631,7 +631,7 @@ def main():
                 "work_per_launch": work[dom][0], "avg_launch_us": kd["avg_us"]}
         par = f"batch-shard x{world}" if tp == 1 else (
             f"kv-head TP x{tp} (row-sharded residual; "
-            f"{'GEMM epilogue scatter over NVLink peer memory' if args.tp_fused else 'NCCL reduce-scatter'} + "
+            f"{'NCCL reduce-scatter' if args.tp_nccl else 'GEMM epilogue scatter over NVLink peer memory'} + "
             f"INT4 NCCL all-gather) x batch-shard x{topo.dp}")
         line = {
             "metric": METRIC, "value": value, "unit": "latents/s", "n_gpus": world, "steps": args.steps,

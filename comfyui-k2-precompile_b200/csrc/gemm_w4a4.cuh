@@ -84,7 +84,7 @@ constexpr int GEMM_SMEM_BYTES = GEMM_OFF_BAR + GEMM_NBARS * 8 + 16 + 1024;  // +
 // packed-A stages: SwiGLU needs two 4 x 128 x 33-float stage buffers and 512
 // floats for the group maxima.
 constexpr int kSwXch = 4 * 128 * 33;
-static_assert(GEMM_OFF_SC >= (2 * kSwXch + 512) * 4, "exchange space");
+static_assert(GEMM_OFF_SC >= (2 * kSwXch + 512) * 4 && GEMM_OFF_SC >= 128 * 260 * 4, "exchange space");
 // Accumulator seed: as fp32 bits, 0x4B400000 + x reads as 12582912 + x for |x| < 2^22.
 constexpr uint32_t kAccBias = 0x4B400000u;
 
@@ -484,18 +484,35 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int col0 = n0 + cq * 64;  // first segment column of this thread (non-SwiGLU kinds)
       const bool col_ok = pairw || col0 < S.n;
       if (S.kind == SEG_F32 || S.kind == SEG_F32_SCATTER) {
-        if (row_ok && col_ok) {
+        // The tile goes through shared memory so that every warp store covers
+        // 512 contiguous bytes of one row: row-per-lane stores would send one
+        // 16-byte transaction per lane, which NVLink (the scatter's peer
+        // stores) carries far below its bandwidth.  Row stride 260 floats
+        // keeps the 16-byte writes of 8 consecutive rows on distinct banks.
+        float* trow = xch + rloc * 260 + cq * 64;
+#pragma unroll
+        for (int i = 0; i < 64; i += 4)
+          *reinterpret_cast<float4*>(trow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+        epi_barrier();
+        const int ew = warp - 4;  // epilogue warp 0..15: rows ew, ew + 16, ...
+        const int vc = min(GEMM_BN, S.n - n0);  // valid columns of this tile
+        for (int rr = ew; rr < GEMM_BM; rr += GEMM_EPI_WARPS) {
+          const int grow = m0 + rr;
+          if (grow >= p.M) break;
           float* o;
           if (S.kind == SEG_F32) {
-            o = reinterpret_cast<float*>(S.out) + (int64_t)row * S.ld + col0;
+            o = reinterpret_cast<float*>(S.out) + (int64_t)grow * S.ld + n0;
           } else {
-            const int dest = row / p.scatter_chunk;
-            o = p.peer[dest] + ((int64_t)p.scatter_rank * p.scatter_chunk + (row - dest * p.scatter_chunk)) * S.ld +
-                col0;
+            const int dest = grow / p.scatter_chunk;
+            o = p.peer[dest] +
+                ((int64_t)p.scatter_rank * p.scatter_chunk + (grow - dest * p.scatter_chunk)) * S.ld + n0;
           }
+          const float* src = xch + rr * 260;
 #pragma unroll
-          for (int i = 0; i < 64; i += 4)
-            *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+          for (int h = 0; h < GEMM_BN; h += 128) {
+            const int c = h + 4 * lane;
+            if (c < vc) *reinterpret_cast<float4*>(o + c) = *reinterpret_cast<const float4*>(src + c);
+          }
         }
 
       } else if (S.kind == SEG_BF16 || S.kind == SEG_SIGMOID) {
