@@ -139,22 +139,6 @@ __device__ __forceinline__ void unpack_chunk(uint4 v, uint4& lo, uint4& hi) {
   lo.w = (v.w << 4) & 0xF0F0F0F0u; hi.w = v.w & 0xF0F0F0F0u;
 }
 
-// Hadamard stages h = 2, 4, 8, 1, 16, 32 (the contract's order without the
-// final h = 64) on 64 consecutive values held by one thread.
-__device__ __forceinline__ void hadamard64_regs(float (&v)[64]) {
-#pragma unroll
-  for (int st = 0; st < 6; ++st) {
-    const int lh = hadamard_stage_bit(st);
-    const int h = 1 << lh;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int lo = ((i >> lh) << (lh + 1)) | (i & (h - 1));
-      const float a = v[lo], b = v[lo + h];
-      v[lo] = __fadd_rn(a, b);
-      v[lo + h] = __fsub_rn(a, b);
-    }
-  }
-}
 
 // Named barrier over the 16 epilogue warps only.
 __device__ __forceinline__ void epi_barrier() {
@@ -381,13 +365,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const bool row_ok = row < p.M;
     const __half* sa_row = p.sa + (int64_t)(row_ok ? row : 0) * G;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    // This thread's TMEM / scale columns: chunks ca, ca+16, cb, cb+16 land in
-    // register slots 0, 16, 32, 48.  SwiGLU: 32 gate columns (ca) and the same
-    // 32 up columns (cb = 128 + ca); other kinds: 64 consecutive columns.
-    // ca: first column; chunk offsets 0, 16, kCd, kCd + 16 from ca
+    // This thread's TMEM / scale columns: chunks ca, ca+16, ca+kCd, ca+kCd+16
+    // land in register slots 0, 16, 32, 48.  SwiGLU: 32 gate columns (ca) and
+    // the same 32 up columns (ca + 128); other kinds: 64 consecutive columns.
     constexpr int kCd = pairw ? GEMM_BN / 2 : 32;
     const int ca = pairw ? 32 * cq : 64 * cq;
-    const int cb = ca + kCd;
     const uint32_t tmem_empty_remote = cluster_map(smem_u32(tmem_empty), 0);
     bool ok = true;
     float2 acc2[32];  // register slots (2j, 2j+1)

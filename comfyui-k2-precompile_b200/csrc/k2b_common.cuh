@@ -319,39 +319,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// 32 lanes x 32 columns of 32-bit.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld_regs32(uint32_t (&r)[32]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
-                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
-                 "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
-                 "+r"(r[30]), "+r"(r[31])
-               :
-               : "memory");
-}
-// Writes the same 32-bit value into 8 consecutive columns of each of the
-// warp's 32 lanes (a wider form would need that many registers holding it).
-__device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
-               : "memory");
-}
-// 64 columns starting at taddr.
-__device__ __forceinline__ void tmem_fill64(uint32_t taddr, uint32_t v) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tmem_fill8(taddr + 8 * i, v);
-}
 __device__ __forceinline__ void setmaxnreg_dec32() { asm volatile("setmaxnreg.dec.sync.aligned.u32 32;"); }
 __device__ __forceinline__ void setmaxnreg_inc112() { asm volatile("setmaxnreg.inc.sync.aligned.u32 112;"); }
 
@@ -547,10 +514,6 @@ __device__ __forceinline__ uint32_t pack8_codes(const uint32_t (&b)[8]) {
 #pragma unroll
   for (int j = 1; j < 8; ++j) s += b[j] << (4 * j);
   return (s - pack_bias8()) ^ 0x88888888u;
-}
-// Two quant_bits words -> one byte of two's-complement nibbles (even low).
-__device__ __forceinline__ uint32_t pack2_codes(uint32_t b0, uint32_t b1) {
-  return (((b1 << 4) + b0) ^ 0x88u) & 0xFFu;
 }
 
 }  // namespace k2b
