@@ -24,6 +24,7 @@ enum DeviceError : int {
   ERR_WAIT_EPILOGUE = 1 << 3,
   ERR_WAIT_SOFTMAX = 1 << 4,
   ERR_WAIT_LOAD = 1 << 5,
+  ERR_WAIT_SELFTEST = 1 << 6,
 };
 
 // Upper bound for any single mbarrier wait.  Normal waits are microseconds.
@@ -83,17 +84,18 @@ constexpr uint32_t kWaitSleepNs = 1000000;  // 1 ms per suspension
 
 // Bounded wait for the completion of phase `parity` of `bar`.  Returns false
 // (after raising *abort and recording `code`) if the CTA was aborted or the
-// wait exceeded kWaitLimitNs.  Between checks the thread sleeps in
-// try_wait (woken by the phase completing), so waiting warps leave the issue
-// slots to the warps doing work.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+// wait exceeded `limit_ns`.  Between checks the thread sleeps in try_wait
+// (woken by the phase completing), so waiting warps leave the issue slots to
+// the warps doing work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = global_timer();
   for (;;) {
     if (mbar_try_wait_sleep(a, parity, kWaitSleepNs)) return true;
     if (*abort_flag) return false;
-    if (global_timer() - t0 > kWaitLimitNs) {
+    if (global_timer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicOr(&g_error, code);
       return false;

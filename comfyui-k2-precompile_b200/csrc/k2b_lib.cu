@@ -303,6 +303,48 @@ static int attention_launch(const void* q, const void* k, const void* v, const v
   return launch_status();
 }
 
+// ------------------------------------------------ bounded-wait self-test
+// Exercises the failure path every kernel's waits share (mbar_wait), on a
+// barrier of its own.  One CTA of two warps:
+//   mode 0: lane 0 of warp 1 completes the barrier warp 0 waits on;
+//   mode 1: nothing completes it, so warp 0 gives up after `limit_ns`
+//           (raising the CTA's abort flag and ERR_WAIT_SELFTEST), while warp 1
+//           waits with a 64x longer limit on a second barrier that nothing
+//           completes, and leaves when it sees the abort flag.
+// result[0] = warp 0's wait succeeded, result[1] = warp 1 left through the
+// abort flag (its wait failed before its own limit), result[2] = warp 1's
+// time in its wait in microseconds.
+__global__ void selftest_wait_kernel(int mode, unsigned long long limit_ns, int* result) {
+  __shared__ __align__(8) uint64_t bar[2];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const bool ok = mbar_wait(&bar[0], 0, &abort_flag, ERR_WAIT_SELFTEST, limit_ns);
+    if (lane == 0) result[0] = ok ? 1 : 0;
+  } else if (mode == 0) {
+    if (lane == 0) {
+      mbar_arrive(&bar[0]);
+      result[1] = 0;
+      result[2] = 0;
+    }
+  } else {
+    const unsigned long long t0 = global_timer();
+    const bool ok = mbar_wait(&bar[1], 0, &abort_flag, ERR_WAIT_SELFTEST, 64 * limit_ns);
+    const unsigned long long dt = global_timer() - t0;
+    if (lane == 0) {
+      result[1] = (!ok && dt < 64 * limit_ns) ? 1 : 0;
+      result[2] = (int)(dt / 1000);
+    }
+  }
+}
+
 }  // namespace k2b
 
 using namespace k2b;
@@ -312,6 +354,16 @@ using namespace k2b;
 // =====================================================================
 
 K2B_EXPORT const char* k2b_version(void) { return "k2b 0.1 sm_100a"; }
+
+// Bounded-wait self-test (see selftest_wait_kernel); `result` is a device
+// int[3].  limit_ns is capped at one second.
+K2B_EXPORT int k2b_selftest_wait(int mode, long long limit_ns, void* result, void* stream) {
+  if ((mode != 0 && mode != 1) || limit_ns <= 0 || limit_ns > 1000000000ll || !result)
+    return (int)cudaErrorInvalidValue;
+  selftest_wait_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(mode, (unsigned long long)limit_ns,
+                                                          static_cast<int*>(result));
+  return launch_status();
+}
 
 K2B_EXPORT int k2b_device_error(int reset, void* stream) {
   int v = 0;

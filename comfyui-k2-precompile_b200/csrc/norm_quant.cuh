@@ -208,66 +208,66 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
           uint4* yo = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(q) + (int64_t)(row0 + r) * K + col);
           yo[0] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
           yo[1] = make_uint4(vw[4], vw[5], vw[6], vw[7]);
-          return;
-        }
-        // layout A: p[k] = (x[2k], x[2k+1]) of this lane's 16 columns
-        float2 p[8];
+        } else {
+          // layout A: p[k] = (x[2k], x[2k+1]) of this lane's 16 columns
+          float2 p[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = bf2_unpack(vw[k]);
+          for (int k = 0; k < 8; ++k) p[k] = bf2_unpack(vw[k]);
 #pragma unroll
-        for (int lk = 0; lk < 3; ++lk) {  // h = 2, 4, 8
+          for (int lk = 0; lk < 3; ++lk) {  // h = 2, 4, 8
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            if (!(k & (1 << lk))) bfly2(p[k], p[k | (1 << lk)]);
-        }
-        __syncwarp();
+            for (int k = 0; k < 8; ++k)
+              if (!(k & (1 << lk))) bfly2(p[k], p[k | (1 << lk)]);
+          }
+          __syncwarp();
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          *reinterpret_cast<float4*>(tra + 4 * k) =
-              make_float4(p[2 * k].x, p[2 * k].y, p[2 * k + 1].x, p[2 * k + 1].y);
-        __syncwarp();
-        // layout B: o[m] = (x[e], x[e+1]), e = 2v + 16m
-        float2 o[8];
-#pragma unroll
-        for (int m = 0; m < 8; ++m)
-          o[m] = *reinterpret_cast<const float2*>(trb + 4 * (4 * m + (m >> 1)));
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {  // h = 1
-          const float a = o[m].x, b = o[m].y;
-          o[m] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
-        }
-#pragma unroll
-        for (int lm = 0; lm < 3; ++lm) {  // h = 16, 32, 64
+          for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<float4*>(tra + 4 * k) =
+                make_float4(p[2 * k].x, p[2 * k].y, p[2 * k + 1].x, p[2 * k + 1].y);
+          __syncwarp();
+          // layout B: o[m] = (x[e], x[e+1]), e = 2v + 16m
+          float2 o[8];
 #pragma unroll
           for (int m = 0; m < 8; ++m)
-            if (!(m & (1 << lm))) bfly2(o[m], o[m | (1 << lm)]);
-        }
-        float amax = 0.0f;
+            o[m] = *reinterpret_cast<const float2*>(trb + 4 * (4 * m + (m >> 1)));
 #pragma unroll
-        for (int m = 0; m < 8; ++m) amax = fmax3(amax, fabsf(o[m].x), fabsf(o[m].y));
-#pragma unroll
-        for (int d = 1; d < 8; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-        const QuantGroup qg = quant_scale(amax);
-        const float c = quant_c_table(qg.sd, s_rcp);
-        const bool clamp = __any_sync(0xffffffffu, qg.clamp);
-        const float2 c2 = make_float2(c, c), mg = make_float2(kRoundMagic8, kRoundMagic8);
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          float2 r2 = __ffma2_rn(o[m], c2, mg);
-          if (clamp) {
-            r2.x = fminf(fmaxf(r2.x, kRoundMagic), kRoundMagic + 15.0f);
-            r2.y = fminf(fmaxf(r2.y, kRoundMagic), kRoundMagic + 15.0f);
+          for (int m = 0; m < 8; ++m) {  // h = 1
+            const float a = o[m].x, b = o[m].y;
+            o[m] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
           }
-          // low byte = offset-8 nibbles (even element low); bits 4..21 of
-          // each word are zero, so the shifted add carries nothing into it
-          cb[cpos + v + 8 * m] = (uint8_t)((__float_as_uint(r2.y) << 4) + __float_as_uint(r2.x));
+#pragma unroll
+          for (int lm = 0; lm < 3; ++lm) {  // h = 16, 32, 64
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+              if (!(m & (1 << lm))) bfly2(o[m], o[m | (1 << lm)]);
+          }
+          float amax = 0.0f;
+#pragma unroll
+          for (int m = 0; m < 8; ++m) amax = fmax3(amax, fabsf(o[m].x), fabsf(o[m].y));
+#pragma unroll
+          for (int d = 1; d < 8; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+          const QuantGroup qg = quant_scale(amax);
+          const float c = quant_c_table(qg.sd, s_rcp);
+          const bool clamp = __any_sync(0xffffffffu, qg.clamp);
+          const float2 c2 = make_float2(c, c), mg = make_float2(kRoundMagic8, kRoundMagic8);
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            float2 r2 = __ffma2_rn(o[m], c2, mg);
+            if (clamp) {
+              r2.x = fminf(fmaxf(r2.x, kRoundMagic), kRoundMagic + 15.0f);
+              r2.y = fminf(fmaxf(r2.y, kRoundMagic), kRoundMagic + 15.0f);
+            }
+            // low byte = offset-8 nibbles (even element low); bits 4..21 of
+            // each word are zero, so the shifted add carries nothing into it
+            cb[cpos + v + 8 * m] = (uint8_t)((__float_as_uint(r2.y) << 4) + __float_as_uint(r2.x));
+          }
+          __syncwarp();
+          uint2 packed = *reinterpret_cast<const uint2*>(cb + cpos + 8 * v);
+          packed.x ^= 0x88888888u;  // offset-8 -> two's-complement nibbles
+          packed.y ^= 0x88888888u;
+          *reinterpret_cast<uint2*>(qp) = packed;
+          if (v == 0) *sp = qg.scale;
         }
-        __syncwarp();
-        uint2 packed = *reinterpret_cast<const uint2*>(cb + cpos + 8 * v);
-        packed.x ^= 0x88888888u;  // offset-8 -> two's-complement nibbles
-        packed.y ^= 0x88888888u;
-        *reinterpret_cast<uint2*>(qp) = packed;
-        if (v == 0) *sp = qg.scale;
       };
       // Two x buffers alternate (row r in A, r+1 in B); each is refilled as
       // soon as its row is consumed, a row ahead, with no register copies.

@@ -20,6 +20,7 @@ _LL = ctypes.c_longlong
 SIGNATURES = {
     "k2b_version": (ctypes.c_char_p, []),
     "k2b_device_error": (_I, [_I, _P]),
+    "k2b_selftest_wait": (_I, [_I, _LL, _P, _P]),
     "k2b_norm_quant": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
     "k2b_rotate_quant": (_I, [_P, _P, _P, _I, _I, _P]),
     "k2b_prepare_weight": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),

@@ -418,8 +418,19 @@ def device_error(reset: bool = True) -> int:
     return int(lib().k2b_device_error(1 if reset else 0, _stream()))
 
 
+def selftest_wait(mode: int, limit_ns: int, device=None) -> list:
+    """Runs the library's bounded-wait self-test (k2b_selftest_wait) on the
+    current stream and returns its int[3] result; mode 1 makes a device wait
+    run out after `limit_ns` without faulting the context."""
+    res = torch.zeros(3, dtype=torch.int32, device=device or torch.device("cuda"))
+    check(lib().k2b_selftest_wait(int(mode), int(limit_ns), _p(res), _stream()), "k2b_selftest_wait")
+    torch.cuda.current_stream(res.device).synchronize()
+    return [int(v) for v in res.cpu()]
+
+
 __all__ = [
     "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_quant_rows", "gated_add", "reduce_gated_add", "norm_mod", "elementwise", "rope", "rotate_quant",
     "gemm_f32", "gemm_f32_scatter", "gemm_bf16", "qkv",
     "gated_residual", "swiglu_quant", "swiglu_bf16", "attention", "attention_quant", "device_error",
+    "selftest_wait",
 ]

@@ -42,6 +42,12 @@ rank's codes are the column slice of the unsharded codes for the same inputs;
 the one numerical difference from one GPU is the fp32 reassociation of the
 projection sums (per-rank partials summed by the reduce-scatter) before the
 bf16 rounding of the projection.
+
+Failure detection is on the host: ``PeerWatch`` is a per-step heartbeat in
+the process group's store, checked before a step launches anything, so a rank
+that raised, exited or stalled between steps is reported on every other rank
+(``PeerLost``) while none of their kernels or collectives is in flight; a
+collective that a peer never joins ends with the process group's own timeout.
 """
 from __future__ import annotations
 
@@ -270,6 +276,56 @@ class PeerSlots:
         self._owned, self._mapped = None, []
 
 
+class PeerLost(RuntimeError):
+    """Raised by PeerWatch.check: the listed ranks did not reach the step."""
+
+    def __init__(self, step: int, ranks: List[int]):
+        super().__init__(f"step {step}: no heartbeat from rank(s) {ranks}")
+        self.step, self.ranks = step, ranks
+
+
+class PeerWatch:
+    """Host-side heartbeat of a group of ranks, one key per rank and step in a
+    torch.distributed store (the process group's, or any shared one).
+
+    ``check(step)`` publishes this rank's heartbeat for ``step`` and waits at
+    most ``timeout_s`` for every peer's; a missing peer raises ``PeerLost``
+    before the caller launches the step, so no GPU work of the survivors
+    waits on it.  Keys of step - 2 are removed as the watch advances."""
+
+    def __init__(self, store, rank: int, ranks: Sequence[int], timeout_s: float = 10.0,
+                 prefix: str = "k2b/alive"):
+        if rank not in ranks:
+            raise ValueError("PeerWatch: rank not in its group")
+        self.store, self.rank, self.ranks = store, rank, list(ranks)
+        self.timeout_s, self.prefix = float(timeout_s), prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def check(self, step: int) -> None:
+        import datetime
+
+        self.store.set(self._key(step, self.rank), "1")
+        peers = [r for r in self.ranks if r != self.rank]
+        try:
+            self.store.wait([self._key(step, r) for r in peers], datetime.timedelta(seconds=self.timeout_s))
+        except Exception as err:  # store timeout, or the store's host is gone
+            missing = []
+            for r in peers:
+                try:
+                    if not self.store.check([self._key(step, r)]):
+                        missing.append(r)
+                except Exception:
+                    missing.append(r)
+            raise PeerLost(step, missing or peers) from err
+        if step >= 2:
+            try:
+                self.store.delete_key(self._key(step - 2, self.rank))
+            except Exception:
+                pass
+
+
 class TPBlocks:
     """One rank's share of a KV-head tensor-parallel block stack.
 
@@ -278,8 +334,9 @@ class TPBlocks:
     form the group's row space, of which this rank holds ``self.shard``."""
 
     def __init__(self, cfg: ModelConfig, blocks: List[BlockWeights], plan: TPPlan, group, batch: int, length: int,
-                 device="cuda", fused: bool = False):
+                 device="cuda", fused: bool = False, watch: Optional[PeerWatch] = None):
         self.cfg, self.blocks, self.plan, self.group = cfg, blocks, plan, group
+        self.watch, self.step = watch, 0
         self.batch, self.length = batch, length
         rows = batch * length
         self.rows = rows
@@ -396,6 +453,9 @@ class TPBlocks:
         len(blocks)*12 + 1 torch.cuda.Event recorded at the phase boundaries
         (PHASES)."""
         self._check(x, freqs, events)
+        if self.watch is not None:  # every peer reached this step: nothing waits on a lost rank
+            self.watch.check(self.step)
+        self.step += 1
         tp, c = self.plan.tp, self.shard.chunk
         for req in self._steps(x, freqs, events):
             if req[0] == "barrier":

@@ -39,8 +39,19 @@ const char* k2b_version(void);
 
 /* Reads (and with reset != 0 clears) the device-side error word: bit 0..5 =
  * a bounded wait in the TMA / MMA / unpack / epilogue / softmax / load role
- * gave up.  Synchronises `stream`.  Returns the word, or -cudaError. */
+ * gave up; bit 6 = the self-test below.  Synchronises `stream`.  Returns the
+ * word, or -cudaError. */
 int k2b_device_error(int reset, void* stream);
+
+/* Self-test of the bounded-wait failure path that every kernel's waits share
+ * (no reference counterpart).  One CTA waits on an mbarrier that, with
+ * mode = 1, nothing completes: the wait gives up after limit_ns (at most one
+ * second) and sets bit 6 of the error word, and a second warp of the CTA
+ * leaves its own endless wait through the CTA's abort flag.  mode = 0 is the
+ * control (the barrier completes).  `result` is a device int[3]: warp 0's
+ * wait succeeded, warp 1 left through the abort flag, warp 1's wait in us.
+ * The context stays usable afterwards. */
+int k2b_selftest_wait(int mode, long long limit_ns, void* result, void* stream);
 
 /* ----------------------------------------------------------- norm_quant --
  * Fused RMSNorm -> adaLN modulation -> H128 rotation -> group-128 INT4.

@@ -208,7 +208,7 @@ def _nccl_rank(rank, world, port, path, fused=False):
     import torch
     import torch.distributed as dist
     from k2b.model import ModelConfig, rope_positions, rope_table, synthetic_blocks
-    from k2b.parallel import TPBlocks, TPPlan, shard_fn, topology
+    from k2b.parallel import PeerWatch, TPBlocks, TPPlan, shard_fn, topology
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dev = torch.device("cuda", rank)
@@ -221,7 +221,8 @@ def _nccl_rank(rank, world, port, path, fused=False):
         topo = topology(world, rank, world)
         plan = TPPlan.of(cfg, world, rank)
         bw = synthetic_blocks(cfg, batch, seed=3, device=dev, shard=shard_fn(plan))
-        m = TPBlocks(cfg, bw, plan, topo.tp_group, batch, length, device=dev, fused=fused)
+        watch = PeerWatch(dist.distributed_c10d._get_default_store(), rank, range(world), timeout_s=30)
+        m = TPBlocks(cfg, bw, plan, topo.tp_group, batch, length, device=dev, fused=fused, watch=watch)
         freqs = rope_table(rope_positions(6, 12, 12), (64, 64)).to(dev)
         rng = np.random.default_rng(4)
         xb = O.bf16_bits(rng.standard_normal((batch * length, cfg.hidden)).astype(np.float32))
