@@ -71,12 +71,11 @@ constexpr int GEMM_LAUNCH_REGS = 96;
 constexpr int GEMM_W_BYTES = GEMM_BN / 2 * 128;   // 16 KB: this CTA's half of the W tile
 constexpr int GEMM_UA_BYTES = GEMM_BM * 128;      // 16 KB
 constexpr int GEMM_PA_BYTES = GEMM_BM * 64;       // 8 KB
-// W scales arrive in chunks of up to 16 K groups, two chunk buffers of 16 KB.
-// The SwiGLU kernel takes chunks of 8: its chunk is two bulk copies per group
-// (gate and up scales), which the producer issues between its W/A copies, and
-// copies from one thread complete one after another, so shorter bursts delay
-// the W/A stream less (gate/up -3.3% measured; the other kinds, one copy per
-// group, were 1.4% slower with 8 and keep 16).
+// W scales arrive in chunks of up to 16 K groups, two chunk buffers of 16 KB,
+// copied by a producer lane of their own.  The SwiGLU kernel (two copies per
+// group: gate and up scales) takes chunks of 4 groups: measured gate/up
+// 14.40 ms with 16, 13.98 with 8, 13.61 with 4, 13.76 with 2; the other kinds
+// are within 0.5% between 8 and 16 and keep 16.
 constexpr int GEMM_SC_MAX_GROUPS = 16;
 constexpr int GEMM_SC_BYTES = GEMM_BN * 4 * GEMM_SC_MAX_GROUPS;
 constexpr int GEMM_OFF_W = 0;
@@ -168,7 +167,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                      const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kScGroups = PAIRW ? 8 : GEMM_SC_MAX_GROUPS;
+  constexpr int kScGroups = PAIRW ? 4 : GEMM_SC_MAX_GROUPS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GEMM_OFF_BAR);
   // full_s[s]: this CTA's W half landed (producer's expect_tx arrival + TMA
   // bytes) and its A unpacked (2 unpacker arrivals); on the leader also the
@@ -266,33 +265,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
           tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
           issued_pa = g + 1;
-          // Scale chunk c (groups 16c .. 16c+15) goes to buffer c % 2: chunks 0
-          // and 1 at the start, chunk c+1 once the producer is 8 groups into
-          // chunk c (the epilogue has then released chunk c-1).
-          const int nchunks = (G + kScGroups - 1) / kScGroups;
-          int chunk = -1;
-          if (g == 0) chunk = 0;
-          else if (g == 1 && nchunks > 1) chunk = 1;
-          else if (g % kScGroups == kScGroups / 2 && g / kScGroups + 1 < nchunks && g >= kScGroups)
-            chunk = g / kScGroups + 1;
-          if (chunk >= 0) {
-            const int cb = chunk & 1;
-            if (chunk >= 2 && !mbar_wait(&empty_sc[cb], ((chunk >> 1) & 1) ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-            const int g0 = chunk * kScGroups;
-            const int ng = min(kScGroups, G - g0);
-            mbar_arrive_expect_tx(&full_sc[cb], ng * (pairw ? GEMM_BN : vcols) * 4);
-            uint8_t* dst = smem + GEMM_OFF_SC + cb * GEMM_SC_BYTES;
-            for (int j = 0; j < ng; ++j) {
-              const int64_t off = (int64_t)(g0 + j) * S.n + n0;
-              if (pairw) {
-                bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 2, &full_sc[cb]);
-                bulk_load(dst + j * GEMM_BN * 4 + GEMM_BN * 2, S.wscale2 + off, GEMM_BN * 2, &full_sc[cb]);
-              } else {
-                bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, (uint32_t)vcols * 4u, &full_sc[cb]);
-              }
+        }
+      } else if (lane == 1) {
+        // ------------------------------------------ W-scale chunk producer
+        // Chunk c (groups kScGroups*c ..) goes to buffer c % 2 once the
+        // epilogue has released chunk c - 2.  A thread of its own: copies
+        // issued by one thread complete one after another, so the scale
+        // copies never queue with the W/A copies of lane 0.
+        const int nchunks = (G + kScGroups - 1) / kScGroups;
+        for (int chunk = 0; chunk < nchunks; ++chunk) {
+          const int cb = chunk & 1;
+          if (chunk >= 2 && !mbar_wait(&empty_sc[cb], ((chunk >> 1) & 1) ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+          const int g0 = chunk * kScGroups;
+          const int ng = min(kScGroups, G - g0);
+          mbar_arrive_expect_tx(&full_sc[cb], ng * (pairw ? GEMM_BN : vcols) * 4);
+          uint8_t* dst = smem + GEMM_OFF_SC + cb * GEMM_SC_BYTES;
+          for (int j = 0; j < ng; ++j) {
+            const int64_t off = (int64_t)(g0 + j) * S.n + n0;
+            if (pairw) {
+              bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 2, &full_sc[cb]);
+              bulk_load(dst + j * GEMM_BN * 4 + GEMM_BN * 2, S.wscale2 + off, GEMM_BN * 2, &full_sc[cb]);
+            } else {
+              bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, (uint32_t)vcols * 4u, &full_sc[cb]);
             }
-            issued_sc = chunk + 1;
           }
+          issued_sc = chunk + 1;
         }
       }
     } else if (warp == 1) {
@@ -677,9 +674,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         mbar_drain(&full_s[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
       for (int g = (issued_pa > GEMM_PSTAGES ? issued_pa - GEMM_PSTAGES : 0); g < issued_pa; ++g)
         mbar_drain(&full_pa[g % GEMM_PSTAGES], (g / GEMM_PSTAGES) & 1);
+    }
+    if (warp == 0 && lane == 1)
       for (int c = (issued_sc > 2 ? issued_sc - 2 : 0); c < issued_sc; ++c)
         mbar_drain(&full_sc[c & 1], (c >> 1) & 1);
-    }
     if (warp == 1 && lane == 0 && issued_mma > 0) {
       const int g = issued_mma - 1;
       mbar_drain(&tmem_full[g & 1], (g >> 1) & 1);
