@@ -201,14 +201,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait(&s_full[t], j & 1, abort_flag, ERR_WAIT_SOFTMAX)) { ok = false; break; }
       tc_fence_after();
+      // all eight loads in flight before one wait (the first wait::ld covers
+      // every load; the others only pin their registers below it)
       float sv[128];
+      {
+        uint32_t u[8][16];
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint32_t u[16];
-        tmem_ld16(lane_base + s_col + 16 * cc, u);
-        tmem_wait_ld_regs(u);
+        for (int cc = 0; cc < 8; ++cc) tmem_ld16(lane_base + s_col + 16 * cc, u[cc]);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sv[16 * cc + i] = __uint_as_float(u[i]);
+        for (int cc = 0; cc < 8; ++cc) {
+          tmem_wait_ld_regs(u[cc]);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sv[16 * cc + i] = __uint_as_float(u[cc][i]);
+        }
       }
       const int valid = p.lk - j * FA_BN;
       if (valid < FA_BN) {
@@ -216,9 +221,16 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= valid) sv[i] = -INFINITY;
       }
-      float mx = sv[0];
+      // row max as eight interleaved chains of 3-input max (exact, order-free)
+      float m8[8];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sv[i]);
+      for (int k = 0; k < 8; ++k) {
+        m8[k] = sv[k];
+#pragma unroll
+        for (int jj = 1; jj < 15; jj += 2) m8[k] = fmax3(m8[k], sv[k + 8 * jj], sv[k + 8 * jj + 8]);
+        m8[k] = fmaxf(m8[k], sv[k + 120]);
+      }
+      const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       float m_use = m_run, alpha = 1.0f;
       bool rescale = false;
       if (j == 0) {
@@ -229,19 +241,21 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         rescale = true;
       }
       const float mc = __fmul_rn(m_use, c);
-      float rowsum = 0.0f;
+      float part[4];  // one partial row sum per 32 columns, summed at the end
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t pk[16];
+        part[cc] = 0.0f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float p0 = fast_exp2(__fmaf_rn(sv[32 * cc + 2 * i], c, -mc));
           const float p1 = fast_exp2(__fmaf_rn(sv[32 * cc + 2 * i + 1], c, -mc));
-          rowsum += p0 + p1;
+          part[cc] += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
         tmem_st16(lane_base + s_col + 16 * cc, pk);
       }
+      const float rowsum = (part[0] + part[1]) + (part[2] + part[3]);
       l_run = __fmaf_rn(l_run, alpha, rowsum);
       m_run = m_use;
       // O of this head is stable here: S_t(j) completing implies PV_t(j-1) completed.

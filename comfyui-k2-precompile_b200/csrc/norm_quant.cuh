@@ -46,12 +46,6 @@ __device__ __forceinline__ void bfly2(float2& a, float2& b) {
   b = __ffma2_rn(b, make_float2(-1.0f, -1.0f), a);
   a = s;
 }
-// max(a, b, c) in one instruction (NaN operands are ignored, as by fmaxf).
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
 // Per-warp transpose buffer: group g (128 fp32) at 144*g floats, logical
 // 16-byte chunk c at chunk c + c/8.  The layout-A stores (lane u of a group
 // writes chunks 4u..4u+3, 8 lanes per wavefront) land on chunks
