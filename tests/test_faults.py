@@ -106,3 +106,23 @@ def test_dropped_collective_ends_with_the_group_timeout(tmp_path):
     assert r0["steps"] == 1 and r0["error"] != "PeerLost"  # the heartbeat of step 1 was there
     assert GROUP_S * 0.5 <= r0["waited"] < GROUP_S + 10
     assert recs[1] == {"rank": 1, "steps": 1}
+
+
+def test_peer_watch_in_one_process():
+    """PeerWatch on an in-process store: a peer's heartbeat present or missing."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from k2b.parallel import PeerLost, PeerWatch
+
+    store = dist.HashStore()
+    store.set_timeout(datetime.timedelta(seconds=5))
+    w0 = PeerWatch(store, 0, [0, 1], timeout_s=0.3)
+    with pytest.raises(PeerLost) as lost:
+        w0.check(0)  # rank 1 never beats
+    assert lost.value.ranks == [1] and lost.value.step == 0
+    PeerWatch(store, 1, [0, 1], timeout_s=0.3).check(0)  # rank 0's key for step 0 is already there
+    w0.check(0)  # now both keys exist
+    with pytest.raises(ValueError):
+        PeerWatch(store, 2, [0, 1])
