@@ -16,9 +16,10 @@
 // (a single-CTA M = 128 MMA measured ~740 cycles per group against ~400 for
 // the pair).  K is consumed one quantisation group per pipeline stage.
 // Roles (640 threads per CTA):
-//   warp 0      TMA producer: packed A group tile (128 x 64 B), this CTA's
-//               half of the prepared W group tile (128 x 128 B, 128B-swizzled);
-//               W scales of all 256 columns in chunks of 16 groups (16 KB)
+//   warp 0      TMA producers: lane 0 the packed A group tile (128 x 64 B)
+//               and this CTA's half of the prepared W group tile (128 x 128 B,
+//               128B-swizzled); lane 1 the W scales of all 256 columns, in
+//               chunks of 4 (SwiGLU) or 16 groups, two chunk buffers
 //   warp 1      TMEM allocator (both CTAs, cta_group::2); leader: single-thread
 //               MMA issuer (4 x K=32 MMAs per group); peer: relays "stage
 //               ready" (W landed + A unpacked) to the leader
