@@ -168,9 +168,13 @@ K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, vo
 // The array is a static device variable: every device that loads the library
 // keeps it for the life of the process.
 //
-// Set-up: the first call on a device (with that device current) resolves the
-// array's device address with cudaGetSymbolAddress; make that first call
-// outside any CUDA stream capture.  Every call shares the one array, and the
+// Address of the array: host code only holds a stand-in for the symbol, so the
+// device address is looked up with cudaGetSymbolAddress in the CUDA context
+// current on the calling thread.  Outside stream capture the lookup runs on
+// every call (it therefore follows a cudaDeviceReset or a different context);
+// during capture the address cached for the current context by an earlier call
+// is used, so the first call in each context must come outside any capture.
+// The cache is guarded by a mutex.  Every call shares the one array, and the
 // kernels overwrite every workspace byte they read (nothing needs to start at
 // zero), so calls whose executions overlap on the GPU (different streams, or
 // different host threads on the same device) race on it and must be
@@ -179,6 +183,58 @@ K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, vo
 namespace k2b {
 constexpr size_t kStaticWorkspaceBytes = size_t(64) << 20;
 static __device__ __align__(256) uint8_t g_static_workspace[kStaticWorkspaceBytes];
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+static CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  return fn;
+}
+
+// Device address of g_static_workspace in the calling thread's current context.
+static int static_workspace_address(cudaStream_t stream, void** out) {
+  static std::mutex mu;
+  static CUcontext ctxs[64];
+  static void* addrs[64];
+  static int used = 0;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+  if (e != cudaSuccess) return (int)e;
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  if (!get) return (int)cudaErrorInitializationError;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cs == cudaStreamCaptureStatusNone) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_workspace);  // also makes the device's context current
+    if (e != cudaSuccess) return (int)e;
+    CUcontext ctx = nullptr;
+    if (get(&ctx) != CUDA_SUCCESS || !ctx) return (int)cudaErrorDeviceUninitialized;
+    int i = 0;
+    while (i < used && ctxs[i] != ctx) ++i;
+    if (i == used) {
+      if (used == 64) i = 0;  // more than 64 contexts: recycle the first entry
+      else ++used;
+    }
+    ctxs[i] = ctx;
+    addrs[i] = p;
+    *out = p;
+    return 0;
+  }
+  CUcontext ctx = nullptr;
+  if (get(&ctx) != CUDA_SUCCESS || !ctx) return (int)cudaErrorDeviceUninitialized;
+  for (int i = 0; i < used; ++i)
+    if (ctxs[i] == ctx) {
+      *out = addrs[i];
+      return 0;
+    }
+  return (int)cudaErrorStreamCaptureUnsupported;  // no call in this context outside capture yet
+}
 }  // namespace k2b
 
 K2B_EXPORT long long k2b_static_workspace_bytes(void) { return (long long)k2b::kStaticWorkspaceBytes; }
@@ -191,17 +247,9 @@ K2B_EXPORT int k2b_forward_blocks_static(const void* const* block_ptrs, int nblo
     return (int)cudaErrorInvalidValue;
   const long long need = k2b_block_workspace_bytes((int)((long long)batch * length), hidden, heads, kvheads, mlp);
   if (need <= 0 || need > (long long)kStaticWorkspaceBytes) return (int)cudaErrorInvalidValue;
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return (int)e;
-  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_workspace);
-    if (e != cudaSuccess) return (int)e;
-    addr[dev] = p;
-  }
-  return k2b_forward_blocks(block_ptrs, nblocks, x, freqs, addr[dev], (long long)kStaticWorkspaceBytes, batch, length,
+  void* ws = nullptr;
+  const int rc = static_workspace_address((cudaStream_t)stream, &ws);
+  if (rc) return rc;
+  return k2b_forward_blocks(block_ptrs, nblocks, x, freqs, ws, (long long)kStaticWorkspaceBytes, batch, length,
                             hidden, heads, kvheads, mlp, eps, qk_eps, nullptr, stream);
 }

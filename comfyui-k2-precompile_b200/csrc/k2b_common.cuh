@@ -416,8 +416,11 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // fp32(1/sqrt(128)), the normalisation of the Sylvester H128 block.
 constexpr float kHadamardScale = 0.0883883461356163024902343750f;
 
-// exp(x): Cody-Waite reduction with a two-part ln2, degree-7 Taylor
-// polynomial in Horner form, exponent-field scaling (oracle: k2o_exp).
+// exp(x): Cody-Waite range reduction x = n*ln2 + r with ln2 split in two
+// parts (the hi/lo split published in fdlibm's e_expf.c: ln2_hi = 0.693145751953125
+// has trailing zero bits so n*ln2_hi is exact), then the degree-7 Taylor
+// polynomial of exp(r) (coefficients 1/k!) in Horner form and exponent-field
+// scaling by 2^n (oracle: k2o_exp).
 __device__ __forceinline__ float exp_contract(float x) {
   if (x != x) return x;
   if (x > 88.72283935546875f) return __int_as_float(0x7f800000);

@@ -9,6 +9,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "../../include/k2b.h"
 #include "attention.cuh"
 #include "gemm_w4a4.cuh"

@@ -227,9 +227,12 @@ int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, cons
  * k2b_forward_blocks with the workspace taken from a file-scope device array
  * of k2b_static_workspace_bytes() (64 MiB; ~1470 token rows at the Krea2
  * widths); larger batch*length is rejected with cudaErrorInvalidValue.  The
- * first call on each device resolves the array's address (cudaGetSymbolAddress)
- * and must come before any stream capture; calls that overlap on the GPU race
- * on the shared array.  Nothing in it needs to start at zero. */
+ * array's device address is looked up (cudaGetSymbolAddress) in the calling
+ * thread's current CUDA context on every call made outside stream capture, so
+ * it follows a cudaDeviceReset or a caller-owned context; during capture the
+ * address cached for that context is used, so the first call in each context
+ * must come before any stream capture.  Calls that overlap on the GPU race on
+ * the shared array.  Nothing in it needs to start at zero. */
 long long k2b_static_workspace_bytes(void);
 int k2b_forward_blocks_static(const void* const* block_ptrs, int nblocks, void* x, const void* freqs, int batch,
                               int length, int hidden, int heads, int kvheads, int mlp, float eps, float qk_eps,

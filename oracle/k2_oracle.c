@@ -336,6 +336,50 @@ int k2o_gemm_w4a4_cols(const uint8_t* A, const uint16_t* sA, const int8_t* wu, c
     return 0;
 }
 
+/* One group step of the dequant above, for callers that form the group's
+ * int32 accumulators elsewhere (oracle.py sums the integer codes of a group
+ * with an fp32 BLAS matmul: every product and partial sum is an integer of
+ * magnitude <= 128*8*8 < 2^24, so the fp32 sum is the exact accumulator in
+ * any order):
+ *     p[i,c] = fmaf(fp32(acc[i,c] * sa[i]), sw[c], p[i,c])
+ * acc, p fp32 [rows, N]; sa fp32 [rows] (this group's activation scales);
+ * sw fp32 [N] (this group's weight scales). */
+static void dequant_group_rows(const float* acc, const float* sa, const float* sw, float* p, int rows, int N) {
+    for (int i = 0; i < rows; ++i) {
+        const float* a = acc + (int64_t)i * N;
+        float* o = p + (int64_t)i * N;
+        const float s = sa[i];
+        for (int c = 0; c < N; ++c) {
+            float u = a[c] * s;
+            o[c] = fmaf(u, sw[c], o[c]);
+        }
+    }
+}
+/* The same loop compiled for CPUs with an FMA unit: fmaf() becomes the
+ * (correctly rounded) fused instruction and the loop vectorises; chosen at run
+ * time, so the library still loads on x86-64-v2 hosts. */
+__attribute__((target("avx2,fma"))) static void dequant_group_rows_fma(const float* acc, const float* sa,
+                                                                        const float* sw, float* p, int rows,
+                                                                        int N) {
+    for (int i = 0; i < rows; ++i) {
+        const float* a = acc + (int64_t)i * N;
+        float* o = p + (int64_t)i * N;
+        const float s = sa[i];
+        for (int c = 0; c < N; ++c) {
+            float u = a[c] * s;
+            o[c] = fmaf(u, sw[c], o[c]);
+        }
+    }
+}
+int k2o_dequant_group(const float* acc, const float* sa, const float* sw, float* p, int rows, int N) {
+    if (rows < 0 || N <= 0) return 1;
+    if (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma"))
+        dequant_group_rows_fma(acc, sa, sw, p, rows, N);
+    else
+        dequant_group_rows(acc, sa, sw, p, rows, N);
+    return 0;
+}
+
 /* ------------------------------------------------------------- epilogues */
 
 /* Per-head RMSNorm over 128 channels with the reduction order of

@@ -66,6 +66,7 @@ def _declare(L):
     L.k2o_norm_mod.argtypes = [P, P, P, P, P, I, I, I, I, I, F]
     L.k2o_unpack_weight.argtypes = [P, P, I, I, P, P]
     L.k2o_gemm_w4a4_cols.argtypes = [P, P, P, P, I, I, I, P, I, I, I, P, I, P]
+    L.k2o_dequant_group.argtypes = [P, P, P, P, I, I]
     L.k2o_qk_norm_rope.argtypes = [P, I, I, I, P, F, P, I, P, P]
     L.k2o_gated_residual.argtypes = [P, I, I, P, P, I, P, P]
     L.k2o_swiglu_quant.argtypes = [P, P, I, I, P, P, P]
@@ -229,12 +230,15 @@ def unpack_weight(W, sW):
 
 def gemm_w4a4(A, sA, W, sW, rows=None, with_acc=False, unpacked=None):
     """Group-scaled W4A4 GEMM.  A u8 [M,K/2], sA fp16 bits [M,K/128], W u8
-    [N,K/2], sW fp16 bits [N,K/128] (or unpacked=(int8 [N,K], fp32 [N,K/128])).
+    [N,K/2], sW fp16 bits [N,K/128] (or unpacked=(int8 or fp32 codes [N,K],
+    fp32 scales [N,K/128])).
     rows: optional row indices.  Returns fp32 [len(rows), N] (and int32
     [len(rows), N, K/128])."""
     A = _c(A, np.uint8)
     sA = _c(sA, np.uint16)
     wu, swf = unpacked if unpacked is not None else unpack_weight(W, sW)
+    if not with_acc:
+        return _gemm_w4a4_blas(A, sA, wu, swf, rows)
     M, K2 = A.shape
     N = wu.shape[0]
     K = K2 * 2
@@ -257,6 +261,42 @@ def gemm_w4a4(A, sA, W, sW, rows=None, with_acc=False, unpacked=None):
     with ThreadPoolExecutor(w) as ex:
         list(ex.map(job, jobs))
     return (out, acc) if with_acc else out
+
+
+def _gemm_w4a4_blas(A, sA, wu, swf, rows):
+    """gemm_w4a4's result with the group accumulators formed by fp32 BLAS
+    matmuls of the integer codes (exact: every partial sum is an integer below
+    2^24 in magnitude) and the dequant chain in C (k2o_dequant_group), group by
+    group in increasing g -- the same fp32 operations as k2o_gemm_w4a4_cols."""
+    if rows is not None:
+        rows = _c(rows, np.int64)
+        A, sA = A[rows], sA[rows]
+    au, saf = unpack_weight(A, sA)
+    n, K = au.shape
+    N = wu.shape[0]
+    G = K // 128
+    af = au.astype(np.float32)
+    # weights may come pre-converted (fp32 codes), like resident GPU weights
+    wf = _c(wu, np.float32) if wu.dtype == np.float32 else _c(wu, np.int8).astype(np.float32)
+    saT = np.ascontiguousarray(saf.T)
+    swT = np.ascontiguousarray(_c(swf, np.float32).T)
+    out = np.zeros((n, N), np.float32)
+    L = lib()
+    w = _workers()
+    rb = max(1, min(n, (1 << 25) // max(1, N)))
+    with ThreadPoolExecutor(w) as ex:
+        for r0 in range(0, n, rb):
+            r1 = min(n, r0 + rb)
+            for g in range(G):
+                acc = np.ascontiguousarray(af[r0:r1, g * 128:(g + 1) * 128] @ wf[:, g * 128:(g + 1) * 128].T)
+
+                def job(ab, acc=acc, r0=r0, g=g):
+                    a, b = ab
+                    assert L.k2o_dequant_group(_p(acc[a:b]), _p(saT[g, r0 + a:r0 + b]), _p(swT[g]),
+                                               _p(out[r0 + a:r0 + b]), b - a, N) == 0
+
+                list(ex.map(job, _row_blocks(r1 - r0, w)))
+    return out
 
 
 def qk_norm_rope(p, heads, normw, eps, freqs, L, rows=None):
@@ -343,23 +383,28 @@ def attention(q, k, v, gate=None, gate_is_sigmoid=True, rows=None):
     c = np.float32(LOG2E / np.sqrt(D))
     out = np.empty((B, rows.size, Hq * D), np.uint16)
     gf = f(gate) if gate is not None else None
-    for b in range(B):
-        for h in range(Hq):
-            kh = h // group
-            s = (qf[b, h, rows].astype(np.float64) @ kf[b, kh].astype(np.float64).T).astype(np.float32)
-            m = s.max(axis=1, keepdims=True)
-            p = np.exp2((s - m) * c).astype(np.float32)
-            l = p.sum(axis=1, dtype=np.float64)
-            pb = bf16_round(p).astype(np.float64)
-            acc = pb @ vf[b, kh].astype(np.float64)
-            o = np.where(l[:, None] == 0, 0.0, acc / np.where(l == 0, 1.0, l)[:, None]).astype(np.float32)
-            ob = bf16_round(o)
-            if gf is not None:
-                g = gf[b, rows, h * D:(h + 1) * D]
-                if not gate_is_sigmoid:
-                    g = bf16_round(1.0 / (1.0 + np.exp(-g.astype(np.float32))))
-                ob = bf16_round(ob * g)
-            out[b, :, h * D:(h + 1) * D] = bf16_bits(ob)
+
+    def head(bh):
+        b, h = bh
+        kh = h // group
+        s = (qf[b, h, rows].astype(np.float64) @ kf[b, kh].astype(np.float64).T).astype(np.float32)
+        m = s.max(axis=1, keepdims=True)
+        p = np.exp2((s - m) * c).astype(np.float32)
+        l = p.sum(axis=1, dtype=np.float64)
+        pb = bf16_round(p).astype(np.float64)
+        acc = pb @ vf[b, kh].astype(np.float64)
+        o = np.where(l[:, None] == 0, 0.0, acc / np.where(l == 0, 1.0, l)[:, None]).astype(np.float32)
+        ob = bf16_round(o)
+        if gf is not None:
+            g = gf[b, rows, h * D:(h + 1) * D]
+            if not gate_is_sigmoid:
+                g = bf16_round(1.0 / (1.0 + np.exp(-g.astype(np.float32))))
+            ob = bf16_round(ob * g)
+        out[b, :, h * D:(h + 1) * D] = bf16_bits(ob)
+
+    # heads are independent; numpy's matmuls and ufuncs release the GIL
+    with ThreadPoolExecutor(max(1, min(8, _workers()))) as ex:
+        list(ex.map(head, [(b, h) for b in range(B) for h in range(Hq)]))
     return out
 
 

@@ -105,3 +105,67 @@ def oracle_block(x_bits, blk, freqs, batch, length, heads, kvheads, eps=1e-6, qk
     hq, hs = O.swiglu_quant(pg, pu)
     pd = O.gemm_w4a4(hq, hs, *blk["wd"])
     return O.gated_residual(pd, mod[5], x1, length)
+
+
+def np_block(b):
+    """A model.BlockWeights (keep_packed=True) as the numpy dict oracle_block takes."""
+    d = {"prenorm": b.prenorm.cpu().numpy(), "postnorm": b.postnorm.cpu().numpy(),
+         "qnorm": b.qnorm.cpu().numpy(), "knorm": b.knorm.cpu().numpy(), "mod": bits(b.mod)}
+    for n, (q, s) in b.packed.items():
+        d[n] = (q.cpu().numpy(), bits(s))
+    return d
+
+
+def stagewise_block(cfg, b, xb, freqs, batch, length, device):
+    """Runs one block stage by stage on the GPU (per-op wrappers) and on the CPU
+    oracle with the same inputs, asserting every integer stage bit-exact and the
+    attention output within TOL_ABS.  Each GPU stage takes the GPU output of the
+    stage before it; after attention the oracle continues from the GPU's
+    attention output (the only stage with a tolerance), so the later integer
+    stages are still compared bit for bit.  Returns (gpu block output bits,
+    stats dict)."""
+    from k2b import ops
+
+    nb = np_block(b)
+    f_np = freqs.cpu().numpy()
+    x = t_bf16(xb, device)
+    mod = nb["mod"]
+    ps, ph, pg, ss, sh, sg = b.mod.unbind(0)
+    rows = batch * length
+    stats = {}
+
+    xq, xs = ops.norm_quant(x, b.prenorm, ps, ph, length=length)
+    xq_r, xs_r = O.norm_quant(xb, nb["prenorm"], mod[0], mod[1], length=length)
+    assert np.array_equal(xq.cpu().numpy(), xq_r) and np.array_equal(bits(xs), xs_r), "norm_quant (pre)"
+    q, k, v, _ = ops.qkv(xq, xs, b.wq, b.wk, b.wv, b.qnorm, b.knorm, freqs, length=length)
+    q_r = O.qk_norm_rope(O.gemm_w4a4(xq_r, xs_r, *nb["wq"]), cfg.heads, nb["qnorm"], cfg.qk_eps, f_np, length)
+    assert np.array_equal(bits(q), q_r), "q projection + QK-norm + RoPE"
+    k_r = O.qk_norm_rope(O.gemm_w4a4(xq_r, xs_r, *nb["wk"]), cfg.kvheads, nb["knorm"], cfg.qk_eps, f_np, length)
+    assert np.array_equal(bits(k), k_r), "k projection + QK-norm + RoPE"
+    v_r = O.bf16_bits(O.gemm_w4a4(xq_r, xs_r, *nb["wv"]))
+    assert np.array_equal(bits(v), v_r), "v projection"
+    shp = lambda t, h: t.view(batch, length, h, 128).transpose(1, 2)
+    o = ops.attention(shp(q, cfg.heads), shp(k, cfg.kvheads), shp(v, cfg.kvheads))
+    t4 = lambda a, h: a.reshape(batch, length, h, 128).transpose(0, 2, 1, 3)
+    o_r = O.attention(t4(q_r, cfg.heads), t4(k_r, cfg.kvheads), t4(v_r, cfg.kvheads)).reshape(rows, -1)
+    o_g = bits(o).reshape(rows, -1)
+    err = float(np.abs(O.bf16_float(o_g) - O.bf16_float(o_r)).max())
+    stats["attention_max_abs"] = err
+    stats["attention_cos"] = cosine(O.bf16_float(o_g), O.bf16_float(o_r))
+    assert err <= TOL_ABS, f"attention max abs {err}"
+    oq, os_ = ops.attention_quant(shp(q, cfg.heads), shp(k, cfg.kvheads), shp(v, cfg.kvheads))
+    oq_r, os_r = O.rotate_quant(o_g)
+    assert np.array_equal(oq.cpu().numpy(), oq_r) and np.array_equal(bits(os_), os_r), "attention INT4 store"
+    x1 = ops.gated_residual(oq, os_, b.wo, pg.contiguous(), x, length=length)
+    x1_r = O.gated_residual(O.gemm_w4a4(oq_r, os_r, *nb["wo"]), mod[2], xb, length)
+    assert np.array_equal(bits(x1), x1_r), "out projection + gated residual"
+    hq_in, hs_in = ops.norm_quant(x1, b.postnorm, ss, sh, length=length)
+    hqi_r, hsi_r = O.norm_quant(x1_r, nb["postnorm"], mod[3], mod[4], length=length)
+    assert np.array_equal(hq_in.cpu().numpy(), hqi_r) and np.array_equal(bits(hs_in), hsi_r), "norm_quant (post)"
+    hq, hs = ops.swiglu_quant(hq_in, hs_in, b.wg, b.wu)
+    hq_r, hs_r = O.swiglu_quant(O.gemm_w4a4(hqi_r, hsi_r, *nb["wg"]), O.gemm_w4a4(hqi_r, hsi_r, *nb["wu"]))
+    assert np.array_equal(hq.cpu().numpy(), hq_r) and np.array_equal(bits(hs), hs_r), "gate/up + SwiGLU + requant"
+    out = ops.gated_residual(hq, hs, b.wd, sg.contiguous(), x1, length=length)
+    out_r = O.gated_residual(O.gemm_w4a4(hq_r, hs_r, *nb["wd"]), mod[5], x1_r, length)
+    assert np.array_equal(bits(out), out_r), "down projection + gated residual"
+    return bits(out), stats

@@ -14,7 +14,7 @@ division, exp -> tl.exp.  The interpreter converts fp32 -> bf16 by truncation
 truncation when comparing.  Nothing of the reference is copied into the
 fixtures except its outputs.
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/ComfyUI-K2-Precompile
 """
 from __future__ import annotations
 
@@ -33,7 +33,9 @@ from triton.language.extra.cuda import libdevice  # noqa: E402
 libdevice.div_rn = lambda a, b, **kw: a / b
 libdevice.exp = lambda a, **kw: tl.exp(a)
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2:
+    raise SystemExit("usage: python tests/golden/make_golden.py /path/to/ComfyUI-K2-Precompile")
+REF = sys.argv[1]
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_triton.npz")
 
 
