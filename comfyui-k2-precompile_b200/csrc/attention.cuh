@@ -47,8 +47,9 @@ struct AttnParams {
   const __nv_bfloat16* gate;        // [B, lq, heads*D] or null
   int gate_kind;                    // 1: apply sigmoid, 2: pre-sigmoided
   __nv_bfloat16* out;               // [B, lq, heads*D] or null
-  uint8_t* oq;                      // [B*lq, heads*D/2] packed or null
+  uint8_t* oq;                      // [B*lq, heads*D/2] packed, [B*lq, heads*D] e4m3 bytes, or null
   __half* os;                       // [B*lq, heads] fp16 scales
+  int oq_bytes;                     // oq holds e4m3 bytes (the block loop's container)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -334,7 +335,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(o[i]));
           const QuantGroup qg = quant_group(amax);
           p.os[orow * p.heads + h] = qg.scale;
-          uint8_t* dq = p.oq + orow * (p.heads * FA_D / 2) + h * 64;
+          const int per_col = p.oq_bytes ? 1 : 0;  // code bytes per column = 2^per_col / 2
+          uint8_t* dq = p.oq + orow * ((p.heads * FA_D) << per_col >> 1) + ((h * 64) << per_col);
 #pragma unroll
           for (int i = 0; i < 128; i += 32) {
             uint32_t w[4];
@@ -345,7 +347,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
               for (int e = 0; e < 8; ++e) b[e] = quant_bits(o[i + 8 * jw + e], qg.c, qg.clamp);
               w[jw] = pack8_codes(b);
             }
-            *reinterpret_cast<uint4*>(dq + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+            if (p.oq_bytes) {
+              uint4 lo, hi;
+              unpack_chunk(make_uint4(w[0], w[1], w[2], w[3]), lo, hi);
+              *reinterpret_cast<uint4*>(dq + i) = lo;
+              *reinterpret_cast<uint4*>(dq + i + 16) = hi;
+            } else {
+              *reinterpret_cast<uint4*>(dq + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
           }
         }
       }

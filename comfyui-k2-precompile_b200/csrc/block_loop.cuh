@@ -13,7 +13,10 @@
 //   down-proj, gated residual with sg     -> x  = x1 + sg * proj
 // Seven launches per block, all on the caller's stream, nothing allocated:
 // the caller passes a workspace of k2b_block_workspace_bytes() bytes.  The
-// sequence is CUDA-graph capturable (no host synchronisation inside).
+// INT4 codes between the kernels (xq, oq, hq) are kept as e4m3 bytes, one per
+// column (the *_e4m3 entry points), so every GEMM loads its A operand with TMA
+// straight into the tensor-core layout.  The sequence is CUDA-graph
+// capturable (no host synchronisation inside).
 
 namespace k2b {
 static inline size_t ws_align(size_t v) { return (v + 255) & ~size_t(255); }
@@ -50,15 +53,16 @@ static BlockWorkspace carve_workspace(uint8_t* base, long long rows, int hidden,
     off += ws_align(n);
     return p;
   };
-  w.xq = take((size_t)rows * hidden / 2);
+  // INT4 codes are kept as e4m3 bytes (one per column) between the kernels
+  w.xq = take((size_t)rows * hidden);
   w.xs = reinterpret_cast<__half*>(take((size_t)rows * (hidden / 128) * 2));
   w.q = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * heads * 128 * 2));
   w.k = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * kvheads * 128 * 2));
   w.v = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * kvheads * 128 * 2));
-  w.oq = take((size_t)rows * heads * 128 / 2);
+  w.oq = take((size_t)rows * heads * 128);
   w.os = reinterpret_cast<__half*>(take((size_t)rows * heads * 2));
   w.x1 = reinterpret_cast<__nv_bfloat16*>(take((size_t)rows * hidden * 2));
-  w.hq = take((size_t)rows * mlp / 2);
+  w.hq = take((size_t)rows * mlp);
   w.hs = reinterpret_cast<__half*>(take((size_t)rows * (mlp / 128) * 2));
   w.bytes = off;
   return w;
@@ -119,31 +123,32 @@ K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, vo
       return rec((CUevent)ev[i], (CUstream)stream) == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidResourceHandle;
     };
     int rc = mark(0);
-    if (!rc) rc = k2b_norm_quant(x, P[K2B_SLOT_PRENORM], ps, ph, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+    if (!rc) rc = k2b_norm_quant_e4m3(x, P[K2B_SLOT_PRENORM], ps, ph, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
     if (!rc) rc = mark(1);
     if (!rc)
-      rc = k2b_qkv(w.xq, w.xs, P[K2B_SLOT_WQ], P[K2B_SLOT_SQ], P[K2B_SLOT_WK], P[K2B_SLOT_SK], P[K2B_SLOT_WV],
+      rc = k2b_qkv_e4m3(w.xq, w.xs, P[K2B_SLOT_WQ], P[K2B_SLOT_SQ], P[K2B_SLOT_WK], P[K2B_SLOT_SK], P[K2B_SLOT_WV],
                    P[K2B_SLOT_SV], nullptr, nullptr, P[K2B_SLOT_QNORM], P[K2B_SLOT_KNORM], freqs, w.q, w.k, w.v,
                    nullptr, m, length, heads * 128, kvheads * 128, hidden, qk_eps, qk_eps, stream);
     if (!rc) rc = mark(2);
     if (!rc)
-      rc = k2b_attention_quant(w.q, w.k, w.v, w.oq, w.os, batch, heads, kvheads, length, length, 128,
+      rc = k2b_attention_quant_e4m3(w.q, w.k, w.v, w.oq, w.os, batch, heads, kvheads, length, length, 128,
                                (long long)length * qst, 128, qst, (long long)length * kst, 128, kst,
                                (long long)length * kst, 128, kst, stream);
     if (!rc) rc = mark(3);
     if (!rc)
-      rc = k2b_gated_residual(w.oq, w.os, P[K2B_SLOT_WO], P[K2B_SLOT_SO], pg, x, w.x1, m, length, hidden,
+      rc = k2b_gated_residual_e4m3(w.oq, w.os, P[K2B_SLOT_WO], P[K2B_SLOT_SO], pg, x, w.x1, m, length, hidden,
                               heads * 128, stream);
     if (!rc) rc = mark(4);
     if (!rc)
-      rc = k2b_norm_quant(w.x1, P[K2B_SLOT_POSTNORM], ss, sh, w.xq, w.xs, m, hidden, length, -1, batch, eps, stream);
+      rc = k2b_norm_quant_e4m3(w.x1, P[K2B_SLOT_POSTNORM], ss, sh, w.xq, w.xs, m, hidden, length, -1, batch, eps,
+                               stream);
     if (!rc) rc = mark(5);
     if (!rc)
-      rc = k2b_swiglu_quant(w.xq, w.xs, P[K2B_SLOT_WG], P[K2B_SLOT_SG], P[K2B_SLOT_WU], P[K2B_SLOT_SU], w.hq, w.hs, m,
+      rc = k2b_swiglu_quant_e4m3(w.xq, w.xs, P[K2B_SLOT_WG], P[K2B_SLOT_SG], P[K2B_SLOT_WU], P[K2B_SLOT_SU], w.hq, w.hs, m,
                             mlp, hidden, stream);
     if (!rc) rc = mark(6);
     if (!rc)
-      rc = k2b_gated_residual(w.hq, w.hs, P[K2B_SLOT_WD], P[K2B_SLOT_SD], sg, w.x1, x, m, length, hidden, mlp,
+      rc = k2b_gated_residual_e4m3(w.hq, w.hs, P[K2B_SLOT_WD], P[K2B_SLOT_SD], sg, w.x1, x, m, length, hidden, mlp,
                               stream);
     if (!rc) rc = mark(7);
     if (rc) return rc;
@@ -162,8 +167,8 @@ K2B_EXPORT int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, vo
 // caller-provided buffer.
 //
 // Limit: kStaticWorkspaceBytes (64 MiB).  With the Krea2 widths (hidden 6144,
-// 48/12 heads, MLP 16384) the workspace takes ~45.5 KB per token row, so up to
-// ~1470 rows (batch * length) per call; larger requests are rejected with
+// 48/12 heads, MLP 16384) the workspace takes ~58.4 KB per token row, so up to
+// ~1120 rows (batch * length) per call; larger requests are rejected with
 // cudaErrorInvalidValue (k2b_static_workspace_bytes() reports the limit).
 // The array is a static device variable: every device that loads the library
 // keeps it for the life of the process.

@@ -1,4 +1,4 @@
-// gemm_w4a4.cuh -- group-scaled W4A4 GEMM on tcgen05 kind::i8 with fused
+// gemm_w4a4.cuh -- group-scaled W4A4 GEMM on tcgen05 kind::f8f6f4 with fused
 // epilogues (dequant, per-head QK RMSNorm + RoPE, sigmoid gate, gated
 // residual, SwiGLU + INT4 requant of the down-projection input).
 //
@@ -6,6 +6,21 @@
 // / residual_norm_kernel (kernels/joint_projection.cu:68-202), the CUTLASS EVT
 // ResidualGemm (kernels/int4_epilogue.cu:18-66) and QKGemm + NormRopeStore
 // (kernels/qk_norm_rope.cu:19-133).
+//
+// Operands: the INT4 codes (-8..7) of both operands are fed to the tensor
+// cores as e4m3 bytes, which hold every code exactly; every product is an
+// integer of magnitude <= 64 and every partial sum of a 128-wide group an
+// integer of magnitude <= 8192, so the fp32 accumulator of a group is the
+// exact integer group sum (the int32 accumulator of an s8 MMA, already in
+// floating point).  kind::f8f6f4 runs at the int8 rate.
+// A (activations) arrives in one of two forms:
+//   BYTEA = false: packed INT4 [M, K/2] (the library's activation contract);
+//               two unpacker warps turn each 128-wide group into e4m3 bytes
+//               in the 128B-swizzled UMMA layout (a byte-permute lookup);
+//   BYTEA = true:  e4m3 bytes [M, K] written by the block loop's producers
+//               (norm_quant, attention, SwiGLU epilogues); TMA loads them
+//               straight into the UMMA layout and the unpackers idle.
+// W is prepared once (k2b_prepare_weight) as e4m3 bytes [N, K].
 //
 // Tile: a CTA pair (cluster of 2 along M) computes 256 rows x 256 columns;
 // each CTA owns 128 rows of A and holds half of the W tile (128 of the 256
@@ -16,23 +31,24 @@
 // (a single-CTA M = 128 MMA measured ~740 cycles per group against ~400 for
 // the pair).  K is consumed one quantisation group per pipeline stage.
 // Roles (640 threads per CTA):
-//   warp 0      TMA producers: lane 0 the packed A group tile (128 x 64 B)
-//               and this CTA's half of the prepared W group tile (128 x 128 B,
-//               128B-swizzled); lane 1 the W scales of all 256 columns, in
-//               chunks of 4 (SwiGLU) or 16 groups, two chunk buffers
+//   warp 0      TMA producers: lane 0 the A group tile (packed 128 x 64 B, or
+//               bytes 128 x 128 B 128B-swizzled) and this CTA's half of the W
+//               group tile (128 x 128 B, 128B-swizzled); lane 1 the W scales
+//               of all 256 columns, in chunks of 4 (SwiGLU) or 16 groups, two
+//               chunk buffers
 //   warp 1      TMEM allocator (both CTAs, cta_group::2); leader: single-thread
 //               MMA issuer (4 x K=32 MMAs per group); peer: relays "stage
 //               ready" (W landed + A unpacked) to the leader
-//   warps 2-3   A unpackers: s4 -> s8 (x16) into the 128B-swizzled UMMA layout
+//   warps 2-3   A unpackers (packed A only): s4 -> e4m3 into the UMMA layout
 //   warps 4-19  epilogue: TMEM lane quadrant = warp % 4, column quarter
 //               = (warp-4)/4 (64 columns of one row per thread)
-// Stage barrier full_s[s] collects this CTA's W bytes (producer expect_tx),
-// its two unpacker arrivals and, on the leader, the peer's relay.  MMA
-// completion is committed to the same barrier offset in both CTAs (multicast
-// commit); the peer's relay and its epilogue warps arrive on the leader's
-// barriers remotely.  TMA copies complete on local barriers only, so each CTA
-// can drain its own copies.
-// TMEM: 2 x 256 int32 columns, one per group in flight (ping-pong), so the MMA
+// Stage barrier full_s[s] collects this CTA's W (and byte A) bytes (producer
+// expect_tx), its two unpacker arrivals (packed A) and, on the leader, the
+// peer's relay.  MMA completion is committed to the same barrier offset in both
+// CTAs (multicast commit); the peer's relay and its epilogue warps arrive on
+// the leader's barriers remotely.  TMA copies complete on local barriers only,
+// so each CTA can drain its own copies.
+// TMEM: 2 x 256 fp32 columns, one per group in flight (ping-pong), so the MMA
 // of group g+1 overlaps the dequant of group g.  The fp32 group sum lives in
 // the epilogue registers (64 per thread); TMEM loads are software-pipelined
 // one 16-column chunk ahead.  setmaxnreg gives the TMA/MMA/unpack warpgroup
@@ -42,15 +58,10 @@
 //
 // Dequant contract (oracle: k2o_gemm_w4a4):
 //   p = 0;  for g:  u = fp32(acc_g * sA[r,g]);  p = fmaf(u, sW[c,g], p)
-// The s8 operands carry 16x the INT4 codes (the nibble is kept in the high
-// half of each byte), so the TMEM accumulator is x = 256*acc_g (|x| <= 2^21).
-// The epilogue turns it into fp32 with an integer add of the exponent bias
-// (bits 0x4B400000 + x read as the float 12582912 + x, exactly) and removes
-// the bias inside the first fma.  (Seeding the accumulator with the bias
-// instead, so the add disappears, costs a TMEM store pass per group and was
-// measured slower.)
-//   u = fma(12582912 + x, sA/256, -12582912*sA/256) = fp32(acc_g * sA)
-// (both sA/256 and 12582912*sA/256 are exact for an fp16-valued sA).
+// With |acc_g| <= 2^13 (at most 13 significant bits) and an fp16 sA (at most
+// 11), acc_g * sA has at most 24 significant bits: u is exact, one fp32
+// multiply of the TMEM word (the exact group sum) by sA.  Both steps run on
+// packed f32x2 pairs.
 #pragma once
 #include "k2b_common.cuh"
 
@@ -91,8 +102,6 @@ constexpr int GEMM_SMEM_BYTES = GEMM_OFF_BAR + GEMM_NBARS * 8 + 16 + 1024;  // +
 // floats for the group maxima.
 constexpr int kSwXch = 4 * 128 * 33;
 static_assert(GEMM_OFF_SC >= (2 * kSwXch + 512) * 4 && GEMM_OFF_SC >= 128 * 260 * 4, "exchange space");
-// Accumulator seed: as fp32 bits, 0x4B400000 + x reads as 12582912 + x for |x| < 2^22.
-constexpr uint32_t kAccBias = 0x4B400000u;
 
 enum SegKind : int {
   SEG_BF16 = 0,       // bf16(p)
@@ -102,7 +111,8 @@ enum SegKind : int {
   SEG_SWIGLU = 4,     // SwiGLU of (gate, up) column pairs + H128 + INT4 requant
   SEG_F32 = 5,        // p itself (tests: exact accumulators)
   SEG_SWIGLU_BF16 = 6,// SwiGLU of (gate, up) column pairs, bf16 h
-  SEG_F32_SCATTER = 7 // p stored into the owner rank's slot of a peer buffer (tensor-parallel partials)
+  SEG_F32_SCATTER = 7,// p stored into the owner rank's slot of a peer buffer (tensor-parallel partials)
+  SEG_SWIGLU_E4M3 = 8 // SEG_SWIGLU with the INT4 codes stored as e4m3 bytes [M, width] (block-loop container)
 };
 
 struct GemmSegment {
@@ -110,12 +120,12 @@ struct GemmSegment {
   int kind;              // SegKind
   int n;                 // columns of the segment's prepared weight(s)
   int ld;                // leading dimension (elements) of the output
-  void* out;             // output base (bf16 / fp32 / packed u8)
+  void* out;             // output base (bf16 / fp32 / packed u8 / e4m3 bytes)
   const float* wscale;   // prepared W scales, fp32 [G, n]
   const float* wscale2;  // SwiGLU: up-projection scales, fp32 [G, n]
   const float* normw;    // SEG_QKNORM: fp32 [128] ("w+1" form)
   float eps;             // SEG_QKNORM
-  __half* out_scale;     // SEG_SWIGLU: fp16 [M, n/128]
+  __half* out_scale;     // SEG_SWIGLU(_E4M3): fp16 [M, n/128]
 };
 
 struct GemmParams {
@@ -138,13 +148,6 @@ struct WeightMaps {
   CUtensorMap m[4];
 };
 
-__device__ __forceinline__ void unpack_chunk(uint4 v, uint4& lo, uint4& hi) {
-  lo.x = (v.x << 4) & 0xF0F0F0F0u; hi.x = v.x & 0xF0F0F0F0u;
-  lo.y = (v.y << 4) & 0xF0F0F0F0u; hi.y = v.y & 0xF0F0F0F0u;
-  lo.z = (v.z << 4) & 0xF0F0F0F0u; hi.z = v.z & 0xF0F0F0F0u;
-  lo.w = (v.w << 4) & 0xF0F0F0F0u; hi.w = v.w & 0xF0F0F0F0u;
-}
-
 
 // Named barrier over the 16 epilogue warps only.
 __device__ __forceinline__ void epi_barrier() {
@@ -161,8 +164,9 @@ __device__ __forceinline__ void store_bf16x64(__nv_bfloat16* o, const float (&v)
 }
 
 // PAIRW: SwiGLU launches (one segment of gate/up column pairs); the column
-// mapping of the epilogue threads is then a compile-time choice.
-template <bool PAIRW>
+// mapping of the epilogue threads is then a compile-time choice.  BYTEA: A is
+// e4m3 bytes [M, K] loaded by TMA (else packed INT4 unpacked in the CTA).
+template <bool PAIRW, bool BYTEA>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w4a4_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ WeightMaps wmaps,
                      const __grid_constant__ GemmParams p) {
@@ -217,7 +221,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < GEMM_STAGES; ++i) {
-      mbar_init(&full_s[i], leader ? 4 : 3);
+      // producer's expect_tx arrival (+ 2 unpacker arrivals for packed A)
+      // (+ the peer's relay on the leader)
+      mbar_init(&full_s[i], (BYTEA ? 1 : 3) + (leader ? 1 : 0));
       mbar_init(&empty_s[i], 1);
     }
     for (int i = 0; i < GEMM_PSTAGES; ++i) {
@@ -258,10 +264,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
           const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
           if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&full_s[s], GEMM_W_BYTES);
+          mbar_arrive_expect_tx(&full_s[s], BYTEA ? GEMM_W_BYTES + GEMM_UA_BYTES : GEMM_W_BYTES);
           // this CTA's 128 of the pair's 256 B columns (SwiGLU: gate | up)
           tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_s[s], g * 128, wrow);
           issued_w = g + 1;
+          if (BYTEA) {
+            // e4m3 A rows of this CTA, straight into the UMMA layout
+            tma_load_2d(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES, &amap, &full_s[s], g * 128, m0);
+            continue;
+          }
           if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pa[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
           mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
           tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
@@ -296,7 +307,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else if (warp == 1) {
       // ------------------------------------- MMA issuer (leader) / relay (peer)
       if (lane == 0 && leader) {
-        constexpr uint32_t idesc = make_idesc(2, 1, 1, 0, 0, 2 * GEMM_BM, GEMM_BN);
+        // fp32 accumulators, e4m3 x e4m3, both K-major
+        constexpr uint32_t idesc = make_idesc(1, 0, 0, 0, 0, 2 * GEMM_BM, GEMM_BN);
         for (int g = 0; g < G; ++g) {
           const int s = g % GEMM_STAGES, b = g & 1;
           const uint32_t ph = (g / GEMM_STAGES) & 1, bph = (g >> 1) & 1;
@@ -309,7 +321,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = umma_desc_sw128(a_base + 32 * k, 16, 1024);
             const uint64_t bd = umma_desc_sw128(w_base + 32 * k, 16, 1024);
-            mma_i8_pair(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
+            mma_f8_pair(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
           }
           mma_commit_pair(&empty_s[s]);
           mma_commit_pair(&tmem_full[b]);
@@ -325,7 +337,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_arrive_remote(ready0 + 8u * (uint32_t)s);
         }
       }
-    } else {
+    } else if (!BYTEA) {
       // ----------------------------------------------------- A unpackers
       const int t = threadIdx.x - 64;  // 0..63
       for (int g = 0; g < G; ++g) {
@@ -335,21 +347,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_UNPACK)) break;
         const uint4* src = reinterpret_cast<const uint4*>(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES);
         uint8_t* dst = smem + GEMM_OFF_UA + s * GEMM_UA_BYTES;
-        // 16-byte chunk i = t + 64*it: row i/4 (= t/4 + 16*it), K columns 32*(i%4) .. +31
+        // 16-byte packed chunk i = t + 64*it: row i/4 (= t/4 + 16*it), K columns
+        // 32*(i%4) .. +31, which land in the row's 16-byte UMMA chunks 2*(i%4)
+        // (columns +0..15) and 2*(i%4)+1 (columns +16..31), XOR-swizzled by row
         const int c = t & 3, r0 = t >> 2;  // (r0 + 16*it) & 7 == r0 & 7
         uint8_t* d0 = dst + r0 * 128 + (((2 * c) ^ (r0 & 7)) << 4);
         uint8_t* d1 = dst + r0 * 128 + (((2 * c + 1) ^ (r0 & 7)) << 4);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint4 pk[4];
+        // two chunks in flight per step: the lookup's temporaries must fit
+        // the 32 registers this warpgroup runs with
 #pragma unroll
-          for (int it = 0; it < 4; ++it) pk[it] = src[t + 64 * (4 * half + it)];
+        for (int part = 0; part < 4; ++part) {
+          uint4 pk[2];
 #pragma unroll
-          for (int it = 0; it < 4; ++it) {
+          for (int it = 0; it < 2; ++it) pk[it] = src[t + 64 * (2 * part + it)];
+#pragma unroll
+          for (int it = 0; it < 2; ++it) {
             uint4 lo, hi;
             unpack_chunk(pk[it], lo, hi);
-            *reinterpret_cast<uint4*>(d0 + (4 * half + it) * 16 * 128) = lo;
-            *reinterpret_cast<uint4*>(d1 + (4 * half + it) * 16 * 128) = hi;
+            *reinterpret_cast<uint4*>(d0 + (2 * part + it) * 16 * 128) = lo;
+            *reinterpret_cast<uint4*>(d1 + (2 * part + it) * 16 * 128) = hi;
           }
         }
         fence_proxy_async_smem();
@@ -389,14 +406,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t s_tfull = smem_u32(tmem_full), s_tempty = smem_u32(tmem_empty);
     const uint32_t s_abort = smem_u32((const void*)abort_flag);
     const uint32_t s_scales = smem_u32(smem + GEMM_OFF_SC) + 4 * ca;
-    auto dequant16 = [&](const uint32_t (&v)[16], uint32_t scs, int slot0, float2 sa2, float2 sb2) {
+    // TMEM words are the exact fp32 group sums: u = acc_g * sA (exact), then
+    // p = fma(u, sW, p), two columns per packed instruction.
+    auto dequant16 = [&](const uint32_t (&v)[16], uint32_t scs, int slot0, float2 sa2) {
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
         const float4 sw = lds128(scs + 4 * i);  // scales of this chunk's columns i .. i+3
-        const float2 u0 = __ffma2_rn(
-            make_float2(__uint_as_float(v[i] + kAccBias), __uint_as_float(v[i + 1] + kAccBias)), sa2, sb2);
-        const float2 u1 = __ffma2_rn(
-            make_float2(__uint_as_float(v[i + 2] + kAccBias), __uint_as_float(v[i + 3] + kAccBias)), sa2, sb2);
+        const float2 u0 = __fmul2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sa2);
+        const float2 u1 = __fmul2_rn(make_float2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])), sa2);
         acc2[(slot0 + i) / 2] = __ffma2_rn(u0, make_float2(sw.x, sw.y), acc2[(slot0 + i) / 2]);
         acc2[(slot0 + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(slot0 + i) / 2 + 1]);
       }
@@ -411,21 +428,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
     for (int g = 0; g < G && ok; ++g) {
       const int b = g & 1, cbuf = (g / kScGroups) & 1;
-      const float sa = row_ok ? __fmul_rn(__half2float(sa_next), 0.00390625f) : 0.0f;
+      const float sa = row_ok ? __half2float(sa_next) : 0.0f;
       if (g + 1 < G) sa_next = sa_row[g + 1];
-      const float sbias = __fmul_rn(sa, -12582912.0f);
-      const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sbias, sbias);
+      const float2 sa2 = make_float2(sa, sa);
       const uint32_t scs = s_scales + cbuf * GEMM_SC_BYTES + (g % kScGroups) * GEMM_BN * 4;
       const uint32_t taddr = tcol + b * GEMM_BN;
       tmem_wait_ld_regs(va);
       tmem_ld16(taddr + 16, vb);
-      dequant16(va, scs, 0, sa2, sb2);
+      dequant16(va, scs, 0, sa2);
       tmem_wait_ld_regs(vb);
       tmem_ld16(taddr + kCd, va);
-      dequant16(vb, scs + 64, 16, sa2, sb2);
+      dequant16(vb, scs + 64, 16, sa2);
       tmem_wait_ld_regs(va);
       tmem_ld16(taddr + kCd + 16, vb);
-      dequant16(va, scs + 4 * kCd, 32, sa2, sb2);
+      dequant16(va, scs + 4 * kCd, 32, sa2);
       tmem_wait_ld_regs(vb);
       // every column of group g is in registers: hand the buffer back to the MMA
       tc_fence_before();
@@ -446,7 +462,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           ok = false;
         }
       }
-      dequant16(vb, scs + 4 * kCd + 64, 48, sa2, sb2);
+      dequant16(vb, scs + 4 * kCd + 64, 48, sa2);
       __syncwarp();
       if (lane == 0 && (g % kScGroups == kScGroups - 1 || g == G - 1))
         mbar_arrive_s(s_empty_sc + 8u * (uint32_t)cbuf);
@@ -657,8 +673,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               for (int e = 0; e < 8; ++e) bits8[e] = quant_bits(hv[8 * j + e], qg.c, qg.clamp);
               w[j] = pack8_codes(bits8);
             }
-            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld + grp * 64 + cq * 16) =
-                make_uint4(w[0], w[1], w[2], w[3]);
+            uint8_t* orow = reinterpret_cast<uint8_t*>(S.out) + (int64_t)row * S.ld;
+            if (S.kind == SEG_SWIGLU_E4M3) {
+              // the same 32 codes as e4m3 bytes, column order
+              uint4 lo, hi;
+              unpack_chunk(make_uint4(w[0], w[1], w[2], w[3]), lo, hi);
+              *reinterpret_cast<uint4*>(orow + grp * 128 + cq * 32) = lo;
+              *reinterpret_cast<uint4*>(orow + grp * 128 + cq * 32 + 16) = hi;
+            } else {
+              *reinterpret_cast<uint4*>(orow + grp * 64 + cq * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
           }
         }
       }

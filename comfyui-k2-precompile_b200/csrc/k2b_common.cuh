@@ -244,6 +244,16 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t d, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The same pair MMA on e4m3 x e4m3 operands with fp32 accumulators
+// (kind::f8f6f4, K = 32 per instruction like kind::i8).
+__device__ __forceinline__ void mma_f8_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, "
+      "p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Completion of the pair's prior MMAs arrives on the mbarrier at this offset
 // in both CTAs.
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
@@ -345,7 +355,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
 }
 
 // Instruction descriptor: c_fmt {0:f16,1:f32,2:s32}, a/b fmt {i8: 0 u8 / 1 s8;
-// f16-kind: 0 f16 / 1 bf16}, majors {0:K, 1:MN}.
+// f16-kind: 0 f16 / 1 bf16; f8f6f4-kind: 0 e4m3 / 1 e5m2}, majors {0:K, 1:MN}.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt, uint32_t a_major,
                                                   uint32_t b_major, uint32_t m, uint32_t n) {
   return (c_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | (a_major << 15) | (b_major << 16) | ((n >> 3) << 17) |
@@ -509,6 +519,27 @@ __device__ __forceinline__ uint32_t quant_bits(float u, float c, bool clamp) {
   float r = __fmaf_rn(u, c, kRoundMagic8);
   if (clamp) r = fminf(fmaxf(r, kRoundMagic), kRoundMagic + 15.0f);
   return __float_as_uint(r);
+}
+// Four INT4 codes (the low 16 bits of w: nibble i = column i, two's
+// complement) -> four e4m3 bytes in column order.  Two byte-permute lookups
+// (codes 0..7 and codes -8..-1, indexed by the nibble's low three bits) and a
+// per-byte select on the nibble's sign bit, itself spread to a byte mask by a
+// third byte-permute.  e4m3(v) for v = 0..7: 00 38 40 44 48 4A 4C 4E; for
+// v = -8..-1: D0 CE CC CA C8 C4 C0 B8.
+__device__ __forceinline__ uint32_t e4m3x4_from_s4x4(uint32_t w) {
+  const uint32_t sel = w & 0x7777u;
+  const uint32_t pos = __byte_perm(0x44403800u, 0x4E4C4A48u, sel);
+  const uint32_t neg = __byte_perm(0xCACCCED0u, 0xB8C0C4C8u, sel);
+  const uint32_t m = __byte_perm(0x0000FF00u, 0u, (w >> 3) & 0x1111u);
+  return (pos & ~m) | (neg & m);
+}
+// 32 packed codes (16 bytes, column order) -> 32 e4m3 bytes: lo = columns
+// 0..15, hi = columns 16..31.
+__device__ __forceinline__ void unpack_chunk(uint4 v, uint4& lo, uint4& hi) {
+  lo = make_uint4(e4m3x4_from_s4x4(v.x), e4m3x4_from_s4x4(v.x >> 16), e4m3x4_from_s4x4(v.y),
+                  e4m3x4_from_s4x4(v.y >> 16));
+  hi = make_uint4(e4m3x4_from_s4x4(v.z), e4m3x4_from_s4x4(v.z >> 16), e4m3x4_from_s4x4(v.w),
+                  e4m3x4_from_s4x4(v.w >> 16));
 }
 // Sum of 0x4B400000 << 4j over j = 0..7, mod 2^32: what the exponent bits of
 // eight quant_bits words add to an 8-nibble shift-and-add pack.

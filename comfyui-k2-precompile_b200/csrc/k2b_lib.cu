@@ -76,7 +76,7 @@ static int make_map_4d_bf16(CUtensorMap* map, const void* base, uint64_t D, uint
 static int launch_status() { return (int)cudaGetLastError(); }
 
 // ----------------------------------------------------------- norm_quant
-template <bool NORM, bool MOD, bool QUANT>
+template <bool NORM, bool MOD, bool QUANT, bool BYTES = false>
 static int norm_quant_launch(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                              int rows, int K, int length, int cut, int batch, float eps, cudaStream_t st,
                              int base_row = 0) {
@@ -96,7 +96,7 @@ static int norm_quant_launch(const void* x, const void* w, const void* scale, co
   int& per_sm = resident[dev];
   if (per_sm == 0) {
     int n = 0, sms = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, norm_quant_kernel<NORM, MOD, QUANT>, kNqThreads, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, norm_quant_kernel<NORM, MOD, QUANT, BYTES>, kNqThreads, 0);
     if (e != cudaSuccess) return (int)e;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return (int)e;
@@ -104,7 +104,7 @@ static int norm_quant_launch(const void* x, const void* w, const void* scale, co
   }
   const int tiles = (rows + kNqRows - 1) / kNqRows;
   const int grid = tiles < per_sm ? tiles : per_sm;
-  norm_quant_kernel<NORM, MOD, QUANT><<<grid, kNqThreads, 0, st>>>(
+  norm_quant_kernel<NORM, MOD, QUANT, BYTES><<<grid, kNqThreads, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(w), static_cast<const __nv_bfloat16*>(scale),
       static_cast<const __nv_bfloat16*>(shift), static_cast<uint8_t*>(q), static_cast<__half*>(s), rows, K, length,
       cut, batch, eps, base_row);
@@ -112,12 +112,12 @@ static int norm_quant_launch(const void* x, const void* w, const void* scale, co
 }
 
 // --------------------------------------------------- weight preparation
-// Packed INT4 [n, k/2] + fp16 group scales [n, k/128] -> s8 [.., k] holding
-// 16*code (same nibble placement as the in-kernel A unpacker) at row
-// dst(r) = (r / block_rows) * dst_block_stride + dst_offset + r % block_rows,
+// Packed INT4 [n, k/2] + fp16 group scales [n, k/128] -> e4m3 bytes [.., k]
+// (the codes in column order, the encoding the in-kernel A unpacker uses) at
+// row dst(r) = (r / block_rows) * dst_block_stride + dst_offset + r % block_rows,
 // and fp32 scales transposed to [k/128, scale_ld] at column dst(r).
 __global__ void prepare_weight_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ ws,
-                                      int8_t* __restrict__ out, float* __restrict__ st, int n, int k, int block_rows,
+                                      uint8_t* __restrict__ out, float* __restrict__ st, int n, int k, int block_rows,
                                       int dst_block_stride, int dst_offset, int scale_ld) {
   const int chunks = k / 32;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -147,9 +147,11 @@ struct SegDesc {
   const void* wscale2;    // SwiGLU: fp32 [K/128, n]
 };
 
+// bytea: `a` is e4m3 bytes [M, K] (the block loop's activation containers)
+// instead of packed INT4 [M, K/2].
 static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDesc* segs, int nseg, int length,
                        const float* freqs, const void* gate, const void* resid, cudaStream_t st,
-                       void* const* peers = nullptr, int tp = 0, int rank = 0, int chunk = 0) {
+                       void* const* peers = nullptr, int tp = 0, int rank = 0, int chunk = 0, bool bytea = false) {
   if (M <= 0 || K <= 0 || K % 128 || nseg < 1 || nseg > 4 || length <= 0) return (int)cudaErrorInvalidValue;
   if (!aligned16(a) || !sa) return (int)cudaErrorInvalidValue;
   CUtensorMap amap;
@@ -160,7 +162,7 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
   int tiles = 0;
   for (int i = 0; i < nseg; ++i) {
     const SegDesc& d = segs[i];
-    const bool pairw = d.kind == SEG_SWIGLU || d.kind == SEG_SWIGLU_BF16;
+    const bool pairw = d.kind == SEG_SWIGLU || d.kind == SEG_SWIGLU_BF16 || d.kind == SEG_SWIGLU_E4M3;
     if (pairw && nseg != 1) return (int)cudaErrorInvalidValue;
     // SwiGLU pairs 128 gate + 128 up columns per tile; other segments take
     // any multiple of 128 columns (a last tile may be half used)
@@ -190,7 +192,8 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     if (d.kind == SEG_QKNORM && (!d.normw || !freqs || !aligned16(freqs))) return (int)cudaErrorInvalidValue;
     if (d.kind == SEG_RESIDUAL && (!gate || !resid || !aligned16(gate) || !aligned16(resid) || d.ld % 8))
       return (int)cudaErrorInvalidValue;
-    if (d.kind == SEG_SWIGLU && (!d.out_scale || d.ld % 16 || !aligned16(d.out))) return (int)cudaErrorInvalidValue;
+    if ((d.kind == SEG_SWIGLU || d.kind == SEG_SWIGLU_E4M3) && (!d.out_scale || d.ld % 16 || !aligned16(d.out)))
+      return (int)cudaErrorInvalidValue;
     if ((d.kind == SEG_BF16 || d.kind == SEG_SIGMOID || d.kind == SEG_QKNORM || d.kind == SEG_SWIGLU_BF16) &&
         (d.ld % 8 || !aligned16(d.out)))
       return (int)cudaErrorInvalidValue;
@@ -198,8 +201,10 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
       return (int)cudaErrorInvalidValue;
     tiles += g.tiles;
   }
-  int rc = make_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, (uint64_t)K / 2, (uint64_t)M, (uint64_t)K / 2, 64,
-                       GEMM_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  int rc = bytea ? make_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128,
+                               GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B)
+                 : make_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, (uint64_t)K / 2, (uint64_t)M, (uint64_t)K / 2,
+                               64, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   p.nseg = nseg;
   p.M = M;
@@ -222,13 +227,16 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     p.scatter_chunk = chunk;
     p.scatter_rank = rank;
   }
-  const bool pairw = segs[0].kind == SEG_SWIGLU || segs[0].kind == SEG_SWIGLU_BF16;
-  void (*kern)(CUtensorMap, WeightMaps, GemmParams) = pairw ? gemm_w4a4_kernel<true> : gemm_w4a4_kernel<false>;
-  static bool attr_set[64][2] = {};
+  const bool pairw = segs[0].kind == SEG_SWIGLU || segs[0].kind == SEG_SWIGLU_BF16 || segs[0].kind == SEG_SWIGLU_E4M3;
+  void (*kern)(CUtensorMap, WeightMaps, GemmParams) =
+      pairw ? (bytea ? gemm_w4a4_kernel<true, true> : gemm_w4a4_kernel<true, false>)
+            : (bytea ? gemm_w4a4_kernel<false, true> : gemm_w4a4_kernel<false, false>);
+  const int variant = (pairw ? 1 : 0) + (bytea ? 2 : 0);
+  static bool attr_set[64][4] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-  if (!attr_set[dev][pairw]) {
+  if (!attr_set[dev][variant]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     // setmaxnreg splits exactly the registers the CTA is launched with: any
@@ -237,7 +245,7 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return (int)e;
     if (fa.numRegs != GEMM_LAUNCH_REGS) return (int)cudaErrorInvalidConfiguration;
-    attr_set[dev][pairw] = true;
+    attr_set[dev][variant] = true;
   }
   // CTA pairs along M (cluster 2 x 1 x 1): 256 rows per pair.
   cudaLaunchConfig_t cfg;
@@ -262,7 +270,8 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
 static int attention_launch(const void* q, const void* k, const void* v, const void* gate, void* out, void* oq,
                             void* os, int batch, int heads, int kvheads, int lq, int lk, int dim, long long q_sb,
                             long long q_sh, long long q_st, long long k_sb, long long k_sh, long long k_st,
-                            long long v_sb, long long v_sh, long long v_st, int gate_kind, cudaStream_t st) {
+                            long long v_sb, long long v_sh, long long v_st, int gate_kind, cudaStream_t st,
+                            bool oq_bytes = false) {
   if (batch <= 0 || heads <= 0 || kvheads <= 0 || heads % kvheads || (heads / kvheads) % 2 || lq <= 0 || lk <= 0 ||
       dim != FA_D)
     return (int)cudaErrorInvalidValue;
@@ -291,6 +300,7 @@ static int attention_launch(const void* q, const void* k, const void* v, const v
   p.out = static_cast<__nv_bfloat16*>(out);
   p.oq = static_cast<uint8_t*>(oq);
   p.os = static_cast<__half*>(os);
+  p.oq_bytes = oq_bytes ? 1 : 0;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -504,7 +514,7 @@ K2B_EXPORT int k2b_prepare_weight(const void* w_packed, const void* w_scale, voi
   const int64_t total = (int64_t)n * (k / 32);
   const int threads = 256;
   prepare_weight_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
-      static_cast<const uint8_t*>(w_packed), static_cast<const __half*>(w_scale), static_cast<int8_t*>(w_prepared),
+      static_cast<const uint8_t*>(w_packed), static_cast<const __half*>(w_scale), static_cast<uint8_t*>(w_prepared),
       static_cast<float*>(scale_t), n, k, block_rows, dst_block_stride, dst_offset, scale_ld);
   return launch_status();
 }
@@ -584,6 +594,63 @@ K2B_EXPORT int k2b_attention_quant(const void* q, const void* k, const void* v, 
                                    long long v_sh, long long v_st, void* stream) {
   return attention_launch(q, k, v, nullptr, nullptr, oq, os, batch, heads, kvheads, lq, lk, dim, q_sb, q_sh, q_st,
                           k_sb, k_sh, k_st, v_sb, v_sh, v_st, 0, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------- e4m3 byte containers
+// The block loop keeps the INT4 codes between its kernels as e4m3 bytes
+// [rows, K] (same codes, one byte each) so that its GEMMs load A with TMA
+// straight into the tensor-core layout; these are the producers and
+// consumers of that container, with the arguments of their packed twins.
+K2B_EXPORT int k2b_norm_quant_e4m3(const void* x, const void* w, const void* scale, const void* shift, void* q8,
+                                   void* s, int rows, int K, int length, int cut, int batch, float eps, void* stream) {
+  return norm_quant_launch<true, true, true, true>(x, w, scale, shift, q8, s, rows, K, length, cut, batch, eps,
+                                                   (cudaStream_t)stream);
+}
+
+K2B_EXPORT int k2b_attention_quant_e4m3(const void* q, const void* k, const void* v, void* oq8, void* os, int batch,
+                                        int heads, int kvheads, int lq, int lk, int dim, long long q_sb,
+                                        long long q_sh, long long q_st, long long k_sb, long long k_sh,
+                                        long long k_st, long long v_sb, long long v_sh, long long v_st,
+                                        void* stream) {
+  return attention_launch(q, k, v, nullptr, nullptr, oq8, os, batch, heads, kvheads, lq, lk, dim, q_sb, q_sh, q_st,
+                          k_sb, k_sh, k_st, v_sb, v_sh, v_st, 0, (cudaStream_t)stream, true);
+}
+
+K2B_EXPORT int k2b_gemm_f32_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, void* out, int m,
+                                 int n, int k, void* stream) {
+  SegDesc d = {SEG_F32, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, true);
+}
+
+K2B_EXPORT int k2b_qkv_e4m3(const void* a8, const void* sa, const void* wq, const void* swq, const void* wk,
+                            const void* swk, const void* wv, const void* swv, const void* wg, const void* swg,
+                            const void* nq, const void* nk, const void* freqs, void* qo, void* ko, void* vo, void* go,
+                            int m, int length, int qwidth, int kvwidth, int k, float eq, float ek, void* stream) {
+  if (qwidth <= 0 || kvwidth <= 0 || qwidth % 128 || kvwidth % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d[4] = {
+      {SEG_QKNORM, qwidth, wq, swq, qo, qwidth, static_cast<const float*>(nq), eq, nullptr, nullptr, nullptr},
+      {SEG_QKNORM, kvwidth, wk, swk, ko, kvwidth, static_cast<const float*>(nk), ek, nullptr, nullptr, nullptr},
+      {SEG_BF16, kvwidth, wv, swv, vo, kvwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+      {SEG_SIGMOID, qwidth, wg, swg, go, qwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+  };
+  const int nseg = (wg && go) ? 4 : 3;
+  return gemm_launch(a8, sa, m, k, d, nseg, length, static_cast<const float*>(freqs), nullptr, nullptr,
+                     (cudaStream_t)stream, nullptr, 0, 0, 0, true);
+}
+
+K2B_EXPORT int k2b_gated_residual_e4m3(const void* a8, const void* sa, const void* w, const void* wscale,
+                                       const void* gate, const void* residual, void* out, int m, int length, int n,
+                                       int k, void* stream) {
+  SegDesc d = {SEG_RESIDUAL, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a8, sa, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                     true);
+}
+
+K2B_EXPORT int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
+                                     const void* su, void* h8, void* hs, int m, int width, int k, void* stream) {
+  if (width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU_E4M3, width, wg, sg, h8, width, nullptr, 0.0f, hs, wu, su};
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, true);
 }
 
 #include "abi_reference.cuh"

@@ -59,7 +59,9 @@ __device__ __forceinline__ constexpr int nq_pad_chunk(int c) { return c + (c >> 
 // NORM: RMS-normalise (y = bf16(x*inv*(w+1))); MOD: then apply the adaLN
 // scale/shift; QUANT: then rotate + INT4 (else store the bf16 row to q).
 //   <1,1,1> norm_quant   <0,0,1> rotate_quant   <1,1,0> norm_mod   <1,0,0> norm
-template <bool NORM, bool MOD, bool QUANT>
+// BYTES (with QUANT): the codes are stored as e4m3 bytes [rows, K], the
+// container the block loop hands to its GEMMs, instead of packed nibbles.
+template <bool NORM, bool MOD, bool QUANT, bool BYTES = false>
 __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bfloat16* __restrict__ x,
                                                                 const float* __restrict__ w,
                                                                 const __nv_bfloat16* __restrict__ scale,
@@ -259,7 +261,12 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
           uint2 packed = *reinterpret_cast<const uint2*>(cb + cpos + 8 * v);
           packed.x ^= 0x88888888u;  // offset-8 -> two's-complement nibbles
           packed.y ^= 0x88888888u;
-          *reinterpret_cast<uint2*>(qp) = packed;
+          if constexpr (BYTES) {  // this lane's 16 columns as e4m3 bytes
+            *reinterpret_cast<uint4*>(qp) = make_uint4(e4m3x4_from_s4x4(packed.x), e4m3x4_from_s4x4(packed.x >> 16),
+                                                       e4m3x4_from_s4x4(packed.y), e4m3x4_from_s4x4(packed.y >> 16));
+          } else {
+            *reinterpret_cast<uint2*>(qp) = packed;
+          }
           if (v == 0) *sp = qg.scale;
         }
       };
@@ -270,17 +277,19 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
         b0 = __ldg(xc + kv);
         b1 = __ldg(xc + kv + 1);
       }
-      uint8_t* qp = q + (int64_t)row0 * (K >> 1) + 256 * i + 8 * lane;
+      // code bytes per row: K/2 packed, or K e4m3 bytes
+      const int qrow = BYTES ? K : (K >> 1);
+      uint8_t* qp = BYTES ? q + (int64_t)row0 * K + col : q + (int64_t)row0 * (K >> 1) + 256 * i + 8 * lane;
       __half* sp = s + (int64_t)row0 * (K >> 7) + 4 * i + g;
       const uint4* xn = xc + 2 * kv;
-      for (int r = 0; r < nrows; r += 2, qp += K, sp += 2 * (K >> 7), xn += 2 * kv) {
+      for (int r = 0; r < nrows; r += 2, qp += 2 * qrow, sp += 2 * (K >> 7), xn += 2 * kv) {
         row_body(a0, a1, r, qp, sp);
         if (r + 2 < nrows) {
           a0 = __ldg(xn);
           a1 = __ldg(xn + 1);
         }
         if (r + 1 < nrows) {
-          row_body(b0, b1, r + 1, qp + (K >> 1), sp + (K >> 7));
+          row_body(b0, b1, r + 1, qp + qrow, sp + (K >> 7));
           if (r + 3 < nrows) {
             b0 = __ldg(xn + kv);
             b1 = __ldg(xn + kv + 1);

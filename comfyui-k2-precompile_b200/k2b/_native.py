@@ -59,6 +59,12 @@ SIGNATURES = {
     "k2_elementwise": (None, [_P] * 4 + [ctypes.c_int64, _I, _I, _I, _P]),
     "k2_rope": (None, [_P] * 5 + [_I] * 7 + [_P]),
     "k2b_shim_status": (_I, [_I]),
+    "k2b_norm_quant_e4m3": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
+    "k2b_attention_quant_e4m3": (_I, [_P] * 5 + [_I] * 6 + [_LL] * 9 + [_P]),
+    "k2b_gemm_f32_e4m3": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "k2b_qkv_e4m3": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
+    "k2b_gated_residual_e4m3": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
+    "k2b_swiglu_quant_e4m3": (_I, [_P] * 8 + [_I, _I, _I, _P]),
 }
 
 _lib = None

@@ -50,7 +50,7 @@ def _cuda(*ts: Optional[torch.Tensor]) -> None:
 class PreparedWeight:
     """Device-resident INT4 weight in the GEMM's streaming layout."""
 
-    w: torch.Tensor      # int8 [n, k] (16 x code, nibble-interleaved per 32 columns)
+    w: torch.Tensor      # uint8 [n, k]: the INT4 codes as e4m3 bytes, column order
     scale: torch.Tensor  # fp32 [k/128, n]
 
     @property
@@ -70,7 +70,7 @@ def prepare_weight(packed: torch.Tensor, scales: torch.Tensor) -> PreparedWeight
     n, k2 = packed.shape
     k = 2 * k2
     _need(k % GROUP == 0 and tuple(scales.shape) == (n, k // GROUP), "weight scale shape mismatch")
-    w = torch.empty((n, k), dtype=torch.int8, device=packed.device)
+    w = torch.empty((n, k), dtype=torch.uint8, device=packed.device)
     s = torch.empty((k // GROUP, n), dtype=torch.float32, device=packed.device)
     check(lib().k2b_prepare_weight(_p(packed), _p(scales), _p(w), _p(s), n, k, n, n, 0, n, _stream()),
           "k2b_prepare_weight")
@@ -414,6 +414,114 @@ def attention_quant(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     return oq, os_
 
 
+# ------------------------------------------------------- e4m3 byte containers
+# The block loop keeps INT4 codes between its kernels as e4m3 bytes [rows, K]
+# (one byte per code, column order): its GEMMs then load A with TMA straight
+# into the tensor-core layout.  These are the per-op forms of that path.
+
+def norm_quant_e4m3(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, *,
+                    length: Optional[int] = None, cut: int = -1, eps: float = 1e-6
+                    ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """norm_quant with the codes as e4m3 bytes: (q8 uint8 [rows, K], s fp16 [rows, K/128])."""
+    _cuda(x, w, scale, shift)
+    _need(x.dtype == torch.bfloat16 and scale.dtype == torch.bfloat16 and shift.dtype == torch.bfloat16 and
+          w.dtype == torch.float32, "norm_quant_e4m3: bf16 x/modulation, fp32 w expected")
+    K = int(x.shape[-1])
+    rows = x.numel() // K
+    if length is None:
+        length = (int(x.shape[-2]) if x.dim() == 3 else rows) or 1
+    batch = max(1, rows // length)
+    _need(w.numel() == K and scale.shape[-1] == K and shift.numel() == scale.numel() and
+          scale.numel() // K >= (2 * batch if cut >= 0 else batch), "norm_quant_e4m3: modulation shape")
+    q = torch.empty((rows, K), dtype=torch.uint8, device=x.device)
+    s = torch.empty((rows, K // GROUP), dtype=torch.float16, device=x.device)
+    if rows:
+        check(lib().k2b_norm_quant_e4m3(_p(x), _p(w), _p(scale), _p(shift), _p(q), _p(s), rows, K, length, cut,
+                                        batch, ctypes.c_float(eps), _stream()), "k2b_norm_quant_e4m3")
+    return q, s
+
+
+def _act8(a: torch.Tensor, sa: torch.Tensor, k: int) -> int:
+    _need(a.dtype == torch.uint8 and sa.dtype == torch.float16, "e4m3 byte activations + fp16 scales expected")
+    _need(a.dim() == 2 and a.shape[1] == k and tuple(sa.shape) == (a.shape[0], k // GROUP),
+          "activation / weight K mismatch")
+    return int(a.shape[0])
+
+
+def gemm_f32_e4m3(a8: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Tensor:
+    """fp32 a@W with A as e4m3 bytes (exact group accumulation)."""
+    _cuda(a8, sa, W.w, W.scale)
+    m = _act8(a8, sa, W.k)
+    out = torch.empty((m, W.n), dtype=torch.float32, device=a8.device)
+    if m:
+        check(lib().k2b_gemm_f32_e4m3(_p(a8), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
+              "k2b_gemm_f32_e4m3")
+    return out
+
+
+def qkv_e4m3(a8, sa, wq: PreparedWeight, wk: PreparedWeight, wv: PreparedWeight, nq, nk, freqs, *, length: int,
+             eps_q: float = 1e-6, eps_k: float = 1e-6, wg: Optional[PreparedWeight] = None):
+    """qkv with A as e4m3 bytes."""
+    _cuda(a8, sa, wq.w, wk.w, wv.w, nq, nk, freqs, None if wg is None else wg.w)
+    m = _act8(a8, sa, wq.k)
+    _need(wk.k == wq.k and wv.k == wq.k and wk.n == wv.n and m % length == 0, "qkv_e4m3: shapes")
+    _need(freqs.dtype == torch.float32 and freqs.numel() == length * 64 * 4, "qkv_e4m3: freqs fp32 [length,64,2,2]")
+    qo = torch.empty((m, wq.n), dtype=torch.bfloat16, device=a8.device)
+    ko = torch.empty((m, wk.n), dtype=torch.bfloat16, device=a8.device)
+    vo = torch.empty((m, wv.n), dtype=torch.bfloat16, device=a8.device)
+    go = None if wg is None else torch.empty((m, wg.n), dtype=torch.bfloat16, device=a8.device)
+    if m:
+        check(lib().k2b_qkv_e4m3(_p(a8), _p(sa), _p(wq.w), _p(wq.scale), _p(wk.w), _p(wk.scale), _p(wv.w),
+                                 _p(wv.scale), _p(None if wg is None else wg.w),
+                                 _p(None if wg is None else wg.scale), _p(nq), _p(nk), _p(freqs), _p(qo), _p(ko),
+                                 _p(vo), _p(go), m, length, wq.n, wk.n, wq.k, ctypes.c_float(eps_q),
+                                 ctypes.c_float(eps_k), _stream()), "k2b_qkv_e4m3")
+    return qo, ko, vo, go
+
+
+def gated_residual_e4m3(a8, sa, W: PreparedWeight, gate: torch.Tensor, residual: torch.Tensor, *,
+                        length: int) -> torch.Tensor:
+    """gated_residual with A as e4m3 bytes."""
+    _cuda(a8, sa, W.w, gate, residual)
+    m = _act8(a8, sa, W.k)
+    _need(residual.numel() == m * W.n and gate.numel() == (m // length) * W.n and m % length == 0,
+          "gated_residual_e4m3: shapes")
+    out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a8.device)
+    if m:
+        check(lib().k2b_gated_residual_e4m3(_p(a8), _p(sa), _p(W.w), _p(W.scale), _p(gate), _p(residual), _p(out),
+                                            m, length, W.n, W.k, _stream()), "k2b_gated_residual_e4m3")
+    return out
+
+
+def swiglu_quant_e4m3(a8, sa, wg: PreparedWeight, wu: PreparedWeight):
+    """Gate/up + SwiGLU + H128 + INT4 with A and h as e4m3 bytes:
+    (h8 uint8 [m, F], hs fp16 [m, F/128])."""
+    _cuda(a8, sa, wg.w, wu.w)
+    m = _act8(a8, sa, wg.k)
+    _need(wu.n == wg.n and wu.k == wg.k, "swiglu weight shapes")
+    F = wg.n
+    h8 = torch.empty((m, F), dtype=torch.uint8, device=a8.device)
+    hs = torch.empty((m, F // GROUP), dtype=torch.float16, device=a8.device)
+    if m:
+        check(lib().k2b_swiglu_quant_e4m3(_p(a8), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(h8),
+                                          _p(hs), m, F, wg.k, _stream()), "k2b_swiglu_quant_e4m3")
+    return h8, hs
+
+
+def attention_quant_e4m3(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    """attention_quant with the codes as e4m3 bytes: (oq8 uint8 [B*L, Hq*128], os fp16 [B*L, Hq])."""
+    qs, ks, vs = _bhld(q, "q"), _bhld(k, "k"), _bhld(v, "v")
+    B, H, L, D = q.shape
+    _need(k.shape[0] == B and k.shape[:3] == v.shape[:3] and H % k.shape[1] == 0, "attention: GQA shapes")
+    oq = torch.empty((B * L, H * D), dtype=torch.uint8, device=q.device)
+    os_ = torch.empty((B * L, H), dtype=torch.float16, device=q.device)
+    if B * L:
+        check(lib().k2b_attention_quant_e4m3(_p(q), _p(k), _p(v), _p(oq), _p(os_), B, H, int(k.shape[1]), L,
+                                             int(k.shape[2]), D, *qs, *ks, *vs, _stream()),
+              "k2b_attention_quant_e4m3")
+    return oq, os_
+
+
 def device_error(reset: bool = True) -> int:
     return int(lib().k2b_device_error(1 if reset else 0, _stream()))
 
@@ -432,5 +540,6 @@ __all__ = [
     "K2BError", "PreparedWeight", "prepare_weight", "norm_quant", "norm_quant_rows", "gated_add", "reduce_gated_add", "norm_mod", "elementwise", "rope", "rotate_quant",
     "gemm_f32", "gemm_f32_scatter", "gemm_bf16", "qkv",
     "gated_residual", "swiglu_quant", "swiglu_bf16", "attention", "attention_quant", "device_error",
-    "selftest_wait",
+    "selftest_wait", "norm_quant_e4m3", "gemm_f32_e4m3", "qkv_e4m3", "gated_residual_e4m3", "swiglu_quant_e4m3",
+    "attention_quant_e4m3",
 ]

@@ -20,9 +20,9 @@
  *   - packed INT4: uint8 [rows, K/2], two codes per byte, low nibble = even
  *     column, plus fp16 scales [rows, K/128]; codes are clamp(rne(v/s),-8,7) of
  *     the Sylvester H128-rotated values, s = fp16(absmax/7);
- *   - prepared weights (k2b_prepare_weight): int8 [n, K] and fp32 scales
- *     [K/128, n]; GEMM dequant: p = sum_g fmaf(fp32(acc_g*sA[r,g]), sW[c,g], .)
- *     in increasing g;
+ *   - prepared weights (k2b_prepare_weight): the codes as e4m3 bytes [n, K]
+ *     and fp32 scales [K/128, n]; GEMM dequant: p = sum_g fmaf(fp32(acc_g *
+ *     sA[r,g]), sW[c,g], .) in increasing g, acc_g the exact group sum;
  *   - RMSNorm weights are fp32 in the "w+1" form (native_schedule.py:252-253).
  */
 #ifndef K2B_H
@@ -102,7 +102,7 @@ int k2b_rope(const void* q, const void* k, const void* f, void* qo, void* ko, in
 /* ---------------------------------------------------- weight preparation --
  * Registration-time conversion of a packed INT4 weight [n, k/2] + fp16 group
  * scales [n, k/128] into the resident layout the GEMM streams with TMA:
- * int8 [.., k] (16 x code, nibble-interleaved per 32 columns) at row
+ * e4m3 bytes [.., k] (each code exactly, column order) at row
  * dst(r) = (r/block_rows)*dst_block_stride + dst_offset + r%block_rows, and
  * fp32 scales [k/128, scale_ld] at column dst(r).  Replaces the per-call
  * weight leases of native_runtime.cpp:84-260 (weights stay resident). */
@@ -200,6 +200,35 @@ int k2b_attention_quant(const void* q, const void* k, const void* v, void* oq, v
                         long long k_sb, long long k_sh, long long k_st, long long v_sb, long long v_sh,
                         long long v_st, void* stream);
 
+/* ------------------------------------------------ e4m3 byte containers --
+ * Forms of the ops above whose INT4 codes travel as e4m3 bytes [rows, K], one
+ * byte per code in column order (e4m3 represents -8..7 exactly), instead of
+ * packed nibbles [rows, K/2]; scales are unchanged.  The native block loop
+ * keeps its intermediate activations in this container so that every GEMM
+ * loads A with TMA straight into the tensor-core layout.  No reference
+ * counterpart (the reference's kernels take packed INT4 only).
+ * k2b_norm_quant_e4m3: k2b_norm_quant with q8 u8 [rows, K];
+ * k2b_attention_quant_e4m3: k2b_attention_quant with oq8 u8 [B*lq, heads*128];
+ * k2b_gemm_f32_e4m3 / k2b_qkv_e4m3 / k2b_gated_residual_e4m3: their packed
+ *   twins with a8 u8 [m, k];
+ * k2b_swiglu_quant_e4m3: a8 u8 [m, k] in, h8 u8 [m, width] + hs out. */
+int k2b_norm_quant_e4m3(const void* x, const void* w, const void* scale, const void* shift, void* q8, void* s,
+                        int rows, int K, int length, int cut, int batch, float eps, void* stream);
+int k2b_attention_quant_e4m3(const void* q, const void* k, const void* v, void* oq8, void* os, int batch, int heads,
+                             int kvheads, int lq, int lk, int dim, long long q_sb, long long q_sh, long long q_st,
+                             long long k_sb, long long k_sh, long long k_st, long long v_sb, long long v_sh,
+                             long long v_st, void* stream);
+int k2b_gemm_f32_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, void* out, int m, int n,
+                      int k, void* stream);
+int k2b_qkv_e4m3(const void* a8, const void* sa, const void* wq, const void* swq, const void* wk, const void* swk,
+                 const void* wv, const void* swv, const void* wg, const void* swg, const void* nq, const void* nk,
+                 const void* freqs, void* qo, void* ko, void* vo, void* go, int m, int length, int qwidth,
+                 int kvwidth, int k, float eq, float ek, void* stream);
+int k2b_gated_residual_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, const void* gate,
+                            const void* residual, void* out, int m, int length, int n, int k, void* stream);
+int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
+                          const void* su, void* h8, void* hs, int m, int width, int k, void* stream);
+
 /* ------------------------------------------------------------ block loop --
  * Native loop over transformer blocks (replaces the compiled entry that
  * NativeGraph::run drives, native_runtime.cpp:543-571, over graph_model.py's
@@ -225,7 +254,7 @@ int k2b_forward_blocks(const void* const* block_ptrs, int nblocks, void* x, cons
  * (an embedding host that owns the device allocator, a plugin handed only its
  * input/output buffers).  No counterpart in the reference: it is
  * k2b_forward_blocks with the workspace taken from a file-scope device array
- * of k2b_static_workspace_bytes() (64 MiB; ~1470 token rows at the Krea2
+ * of k2b_static_workspace_bytes() (64 MiB; ~1120 token rows at the Krea2
  * widths); larger batch*length is rejected with cudaErrorInvalidValue.  The
  * array's device address is looked up (cudaGetSymbolAddress) in the calling
  * thread's current CUDA context on every call made outside stream capture, so

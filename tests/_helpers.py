@@ -169,3 +169,21 @@ def stagewise_block(cfg, b, xb, freqs, batch, length, device):
     out_r = O.gated_residual(O.gemm_w4a4(hq_r, hs_r, *nb["wd"]), mod[5], x1_r, length)
     assert np.array_equal(bits(out), out_r), "down projection + gated residual"
     return bits(out), stats
+
+
+# e4m3 encodings of the INT4 codes -8..7 (index code + 8): the byte container
+# of the block loop and of the prepared weights
+E4M3 = np.array([0xD0, 0xCE, 0xCC, 0xCA, 0xC8, 0xC4, 0xC0, 0xB8,
+                 0x00, 0x38, 0x40, 0x44, 0x48, 0x4A, 0x4C, 0x4E], np.uint8)
+
+
+def unpack_codes(packed):
+    """packed u8 [rows, K/2] -> int codes [rows, K] (low nibble = even column)."""
+    p = np.asarray(packed, np.uint8)
+    c = np.empty((p.shape[0], p.shape[1] * 2), np.int16)
+    c[:, 0::2], c[:, 1::2] = p & 0xF, p >> 4
+    return np.where(c >= 8, c - 16, c)
+
+
+def e4m3_bytes(packed):
+    return E4M3[unpack_codes(packed) + 8]

@@ -56,3 +56,20 @@ def test_norm_weight_w_plus_one_form_is_exact():
     w_eff = w + 1.0
     assert torch.equal(w_eff, w_eff.to(torch.bfloat16).to(torch.float32))
     assert float(w_eff.min()) >= 0.89 and float(w_eff.max()) <= 1.11
+
+
+def test_e4m3_code_table_matches_torch_float8():
+    """The byte-permute lookup tables of the INT4 -> e4m3 conversion (shared by
+    the GEMM's A unpacker, the weight preparation and the byte-container
+    producers) hold torch's e4m3fn encodings of the codes -8..7."""
+    import torch
+
+    from _helpers import E4M3
+
+    ref = torch.arange(-8, 8, dtype=torch.float32).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert (E4M3 == ref).all()
+    # the words of the CUDA lookup: bytes 0..7 of the positive table = e4m3(0..7),
+    # of the negative table = e4m3(-8..-1)
+    pos = (0x44403800).to_bytes(4, "little") + (0x4E4C4A48).to_bytes(4, "little")
+    neg = (0xCACCCED0).to_bytes(4, "little") + (0xB8C0C4C8).to_bytes(4, "little")
+    assert list(pos) == list(ref[8:]) and list(neg) == list(ref[:8])
