@@ -300,31 +300,33 @@ def run_kernel_case(args):
     x = torch.randn((rows, H), generator=g, device=dev).to(torch.bfloat16)
     w = torch.zeros(H, device=dev)
     mod = (torch.randn((6, 1, H), generator=g, device=dev) * 0.1).to(torch.bfloat16)
-    xq, xs = ops.norm_quant(x, w, mod[0], mod[1])
+    # the block loop's forms: INT4 codes in e4m3 byte containers between kernels
+    xq, xs = ops.norm_quant_e4m3(x, w, mod[0], mod[1])
     name = args.kernel
     if name == "norm_quant":
-        fn = lambda: ops.norm_quant(x, w, mod[0], mod[1])
+        fn = lambda: ops.norm_quant_e4m3(x, w, mod[0], mod[1])
     elif name == "qkv":
         wq, wk, wv = weight(cfg.heads * 128, H), weight(cfg.kvheads * 128, H), weight(cfg.kvheads * 128, H)
         L = rows
         freqs = rope_table(rope_positions(L % 64, L // 64, 64), (64, 64)).to(dev)
         nw = torch.zeros(128, device=dev)
-        fn = lambda: ops.qkv(xq, xs, wq, wk, wv, nw, nw, freqs, length=L)
+        fn = lambda: ops.qkv_e4m3(xq, xs, wq, wk, wv, nw, nw, freqs, length=L)
     elif name == "out_proj":
         wo = weight(H, H)
-        fn = lambda: ops.gated_residual(xq, xs, wo, mod[2], x, length=rows)
+        fn = lambda: ops.gated_residual_e4m3(xq, xs, wo, mod[2], x, length=rows)
     elif name == "gate_up":
         wg, wu = weight(F, H), weight(F, H)
-        fn = lambda: ops.swiglu_quant(xq, xs, wg, wu)
+        fn = lambda: ops.swiglu_quant_e4m3(xq, xs, wg, wu)
     elif name == "down":
         wd = weight(H, F)
-        hq = torch.randint(0, 256, (rows, F // 2), dtype=torch.uint8, device=dev)
+        codes = torch.randint(-8, 8, (rows, F), device=dev).to(torch.float32)
+        hq = codes.to(torch.float8_e4m3fn).view(torch.uint8)
         hs = torch.full((rows, F // 128), 0.01, dtype=torch.float16, device=dev)
-        fn = lambda: ops.gated_residual(hq, hs, wd, mod[5], x, length=rows)
+        fn = lambda: ops.gated_residual_e4m3(hq, hs, wd, mod[5], x, length=rows)
     elif name == "attention":
         q = torch.randn((1, cfg.heads, rows, 128), device=dev).to(torch.bfloat16)
         k = torch.randn((1, cfg.kvheads, rows, 128), device=dev).to(torch.bfloat16)
-        fn = lambda: ops.attention_quant(q, k, k)
+        fn = lambda: ops.attention_quant_e4m3(q, k, k)
     else:
         raise SystemExit(f"unknown kernel {name}")
     fn()

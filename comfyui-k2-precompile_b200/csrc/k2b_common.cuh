@@ -82,6 +82,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 constexpr uint32_t kWaitSleepNs = 1000000;  // 1 ms per suspension
 
+// Bounded waits.  Reading %globaltimer costs a few hundred cycles, which on
+// the MMA <-> epilogue handoff chain of the GEMM is paid every K group (traced:
+// ~300 cycles per wait).  So every wait polls first and only starts its clock
+// after kWaitPollsPerCheck failed polls, then looks at the clock once per
+// kWaitPollsPerCheck polls: a wait that completes within a few polls never
+// reads the timer, and every wait still gives up within its limit (plus at
+// most kWaitPollsPerCheck suspended polls).
+constexpr uint32_t kWaitPollsPerCheck = 16;
+
 // Bounded wait for the completion of phase `parity` of `bar`.  Returns false
 // (after raising *abort and recording `code`) if the CTA was aborted or the
 // wait exceeded `limit_ns`.  Between checks the thread sleeps in try_wait
@@ -91,14 +100,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           unsigned long long limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  const unsigned long long t0 = global_timer();
-  for (;;) {
+  unsigned long long t0 = 0;
+  for (uint32_t polls = 1;; ++polls) {
     if (mbar_try_wait_sleep(a, parity, kWaitSleepNs)) return true;
     if (*abort_flag) return false;
-    if (global_timer() - t0 > limit_ns) {
-      *abort_flag = 1;
-      atomicOr(&g_error, code);
-      return false;
+    if (polls % kWaitPollsPerCheck == 0) {
+      const unsigned long long now = global_timer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicOr(&g_error, code);
+        return false;
+      }
     }
   }
 }
@@ -107,16 +121,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // loops that cannot spare registers for generic pointers.
 __device__ __forceinline__ bool mbar_wait_s(uint32_t a, uint32_t parity, uint32_t abort_addr, int code) {
   if (mbar_try_wait(a, parity)) return true;
-  const unsigned long long t0 = global_timer();
-  for (;;) {
+  unsigned long long t0 = 0;
+  for (uint32_t polls = 1;; ++polls) {
     if (mbar_try_wait_sleep(a, parity, kWaitSleepNs)) return true;
     int ab;
     asm volatile("ld.volatile.shared.b32 %0, [%1];" : "=r"(ab) : "r"(abort_addr) : "memory");
     if (ab) return false;
-    if (global_timer() - t0 > kWaitLimitNs) {
-      asm volatile("st.volatile.shared.b32 [%0], %1;" ::"r"(abort_addr), "r"(1) : "memory");
-      atomicOr(&g_error, code);
-      return false;
+    if (polls % kWaitPollsPerCheck == 0) {
+      const unsigned long long now = global_timer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        asm volatile("st.volatile.shared.b32 [%0], %1;" ::"r"(abort_addr), "r"(1) : "memory");
+        atomicOr(&g_error, code);
+        return false;
+      }
     }
   }
 }
@@ -132,8 +151,8 @@ __device__ __forceinline__ float4 lds128(uint32_t a) {
 // mbar_wait for phases completed by arrivals from the other CTA of the pair.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   const uint32_t a = smem_u32(bar);
-  const unsigned long long t0 = global_timer();
-  for (;;) {
+  unsigned long long t0 = 0;
+  for (uint32_t polls = 0;; ++polls) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
@@ -143,10 +162,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         : "memory");
     if (ok) return true;
     if (*abort_flag) return false;
-    if (global_timer() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      atomicOr(&g_error, code);
-      return false;
+    if (polls % kWaitPollsPerCheck == kWaitPollsPerCheck - 1) {
+      const unsigned long long now = global_timer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicOr(&g_error, code);
+        return false;
+      }
     }
   }
 }
