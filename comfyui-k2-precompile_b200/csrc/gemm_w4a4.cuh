@@ -39,7 +39,9 @@
 //   warp 1      TMEM allocator (both CTAs, cta_group::2); leader: single-thread
 //               MMA issuer (4 x K=32 MMAs per group); peer: relays "stage
 //               ready" (W landed + A unpacked) to the leader
-//   warps 2-3   A unpackers (packed A only): s4 -> e4m3 into the UMMA layout
+//   warps 2-3   A unpackers (packed A): s4 -> e4m3 into the UMMA layout;
+//               byte A: lane 0 of warp 2 issues the A tensor copies (a second
+//               issuing thread: one thread's copies complete one at a time)
 //   warps 4-19  epilogue: TMEM lane quadrant = warp % 4, column quarter
 //               = (warp-4)/4 (64 columns of one row per thread)
 // Stage barrier full_s[s] collects this CTA's W (and byte A) bytes (producer
@@ -221,9 +223,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < GEMM_STAGES; ++i) {
-      // producer's expect_tx arrival (+ 2 unpacker arrivals for packed A)
-      // (+ the peer's relay on the leader)
-      mbar_init(&full_s[i], (BYTEA ? 1 : 3) + (leader ? 1 : 0));
+      // W producer's expect_tx arrival + (byte A) the A producer's expect_tx
+      // arrival or (packed A) 2 unpacker arrivals (+ the peer's relay on the
+      // leader)
+      mbar_init(&full_s[i], (BYTEA ? 2 : 3) + (leader ? 1 : 0));
       mbar_init(&empty_s[i], 1);
     }
     for (int i = 0; i < GEMM_PSTAGES; ++i) {
@@ -264,15 +267,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
           const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
           if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&full_s[s], BYTEA ? GEMM_W_BYTES + GEMM_UA_BYTES : GEMM_W_BYTES);
+          mbar_arrive_expect_tx(&full_s[s], GEMM_W_BYTES);
           // this CTA's 128 of the pair's 256 B columns (SwiGLU: gate | up)
           tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_s[s], g * 128, wrow);
           issued_w = g + 1;
-          if (BYTEA) {
-            // e4m3 A rows of this CTA, straight into the UMMA layout
-            tma_load_2d(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES, &amap, &full_s[s], g * 128, m0);
-            continue;
-          }
+          if (BYTEA) continue;  // A comes from the A producer (warp 2)
           if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pa[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
           mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
           tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
@@ -337,7 +336,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_arrive_remote(ready0 + 8u * (uint32_t)s);
         }
       }
-    } else if (!BYTEA) {
+    } else if (BYTEA) {
+      // --------------------------------------------- A producer (byte A)
+      // A tensor copies go out from a warp of their own: copies issued by one
+      // thread complete one after another (~545 cycles each, nearly
+      // independent of size), so one thread issuing both the W and the A copy
+      // of every group would hold the K-group period above ~1100 cycles.
+      if (warp == 2 && lane == 0) {
+        for (int g = 0; g < G; ++g) {
+          const int s = g % GEMM_STAGES;
+          const uint32_t ph = (g / GEMM_STAGES) & 1;
+          if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full_s[s], GEMM_UA_BYTES);
+          // e4m3 A rows of this CTA, straight into the UMMA layout
+          tma_load_2d(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES, &amap, &full_s[s], g * 128, m0);
+          issued_pa = g + 1;
+        }
+      }
+    } else {
       // ----------------------------------------------------- A unpackers
       const int t = threadIdx.x - 64;  // 0..63
       for (int g = 0; g < G; ++g) {
@@ -700,6 +716,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int g = (issued_pa > GEMM_PSTAGES ? issued_pa - GEMM_PSTAGES : 0); g < issued_pa; ++g)
         mbar_drain(&full_pa[g % GEMM_PSTAGES], (g / GEMM_PSTAGES) & 1);
     }
+    if (BYTEA && warp == 2 && lane == 0)
+      for (int g = (issued_pa > GEMM_STAGES ? issued_pa - GEMM_STAGES : 0); g < issued_pa; ++g)
+        mbar_drain(&full_s[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
     if (warp == 0 && lane == 1)
       for (int c = (issued_sc > 2 ? issued_sc - 2 : 0); c < issued_sc; ++c)
         mbar_drain(&full_sc[c & 1], (c >> 1) & 1);
