@@ -22,6 +22,17 @@
 //               straight into the UMMA layout and the unpackers idle.
 // W is prepared once (k2b_prepare_weight) as e4m3 bytes [N, K].
 //
+// Reference-contract modes (the data the reference's kernel library receives
+// through its own symbol names): one fp32 scale per activation row and per
+// weight channel, so the accumulator runs over the whole of K and is scaled
+// once, p = fp32(fp32(acc * xs[r]) * ws[c]) (kernels/joint_projection.cu:57-59):
+//   GM_REF4:  packed INT4 A and packed INT4 W (a checkpoint's ConvRot W4A4
+//             weight as it is stored); W is turned into e4m3 in the CTA by the
+//             epilogue warps, idle until the last group;
+//   GM_REF8:  int8 A and W bytes (kind::i8, int32 accumulator);
+//   GM_REFF8: fp8 A and W bytes, e4m3 or e5m2 (fp32 accumulator), scales
+//             given per row / channel or as one value (stride 0).
+//
 // Tile: a CTA pair (cluster of 2 along M) computes 256 rows x 256 columns;
 // each CTA owns 128 rows of A and holds half of the W tile (128 of the 256
 // columns; for SwiGLU the leader holds the gate rows, the peer the up rows).
@@ -97,7 +108,9 @@ constexpr int GEMM_OFF_UA = GEMM_OFF_W + GEMM_STAGES * GEMM_W_BYTES;
 constexpr int GEMM_OFF_PA = GEMM_OFF_UA + GEMM_STAGES * GEMM_UA_BYTES;
 constexpr int GEMM_OFF_SC = GEMM_OFF_PA + GEMM_PSTAGES * GEMM_PA_BYTES;
 constexpr int GEMM_OFF_BAR = GEMM_OFF_SC + 2 * GEMM_SC_BYTES;
-constexpr int GEMM_NBARS = 2 * GEMM_STAGES + 2 * GEMM_PSTAGES + 2 * 2 + 4;
+constexpr int GEMM_NBARS = 2 * GEMM_STAGES + 2 * GEMM_PSTAGES + 2 * 2 + 4 + 2 * GEMM_PSTAGES;
+constexpr int GEMM_PW_BYTES = 128 * 64;  // packed W rows of one CTA and group (reference contract)
+static_assert(GEMM_PSTAGES * GEMM_PW_BYTES <= 2 * GEMM_SC_BYTES, "packed W stages use the scale-chunk space");
 constexpr int GEMM_SMEM_BYTES = GEMM_OFF_BAR + GEMM_NBARS * 8 + 16 + 1024;  // + alignment slack
 // The final epilogue exchanges rows through the (then idle) W, unpacked-A and
 // packed-A stages: SwiGLU needs two 4 x 128 x 33-float stage buffers and 512
@@ -130,6 +143,14 @@ struct GemmSegment {
   __half* out_scale;     // SEG_SWIGLU(_E4M3): fp16 [M, n/128]
 };
 
+enum GemmMode : int {
+  GM_PACKED = 0,  // group-128 contract, packed INT4 A
+  GM_BYTES = 1,   // group-128 contract, e4m3 byte A
+  GM_REF4 = 2,    // reference contract, packed INT4 A and W
+  GM_REF8 = 3,    // reference contract, int8 A and W
+  GM_REFF8 = 4    // reference contract, fp8 A and W
+};
+
 struct GemmParams {
   GemmSegment seg[4];
   int nseg;
@@ -144,6 +165,13 @@ struct GemmParams {
   // takes it in slot scatter_rank at row r % scatter_chunk
   float* peer[4];
   int scatter_chunk, scatter_rank;
+  // reference-contract modes: activation scales xs[r * xs_stride], weight
+  // scales seg.wscale[c * ws_stride] (fp32), optional fp32 bias [n], and the
+  // fp8 operand formats (GM_REFF8: a | b << 3, 0 e4m3 / 1 e5m2)
+  const float* xs;
+  int xs_stride, ws_stride;
+  const float* bias;
+  uint32_t f8fmt;
 };
 
 struct WeightMaps {
@@ -166,15 +194,19 @@ __device__ __forceinline__ void store_bf16x64(__nv_bfloat16* o, const float (&v)
 }
 
 // PAIRW: SwiGLU launches (one segment of gate/up column pairs); the column
-// mapping of the epilogue threads is then a compile-time choice.  BYTEA: A is
-// e4m3 bytes [M, K] loaded by TMA (else packed INT4 unpacked in the CTA).
-template <bool PAIRW, bool BYTEA>
+// mapping of the epilogue threads is then a compile-time choice.  MODE: a
+// GemmMode (operand forms and scale contract).
+template <bool PAIRW, int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w4a4_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ WeightMaps wmaps,
                      const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kScGroups = PAIRW ? 4 : GEMM_SC_MAX_GROUPS;
+  // A arrives as bytes loaded by TMA (else packed INT4 unpacked by warps 2-3)
+  constexpr bool BYTEA = MODE == GM_BYTES || MODE == GM_REF8 || MODE == GM_REFF8;
+  constexpr bool REF = MODE >= GM_REF4;  // full-K accumulation, per-row / per-channel scales
+  constexpr bool PW = MODE == GM_REF4;   // packed W, unpacked by the epilogue warps
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GEMM_OFF_BAR);
   // full_s[s]: this CTA's W half landed (producer's expect_tx arrival + TMA
   // bytes) and its A unpacked (2 unpacker arrivals); on the leader also the
@@ -187,6 +219,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* empty_sc = full_sc + 2;                 // [2] epilogue done with a scale chunk
   uint64_t* tmem_full = empty_sc + 2;               // [2] MMAs of a group done (both CTAs)
   uint64_t* tmem_empty = tmem_full + 2;             // [2] leader: buffer drained by both CTAs
+  uint64_t* full_pw = tmem_empty + 2;               // [PSTAGES] GM_REF4: packed W landed
+  uint64_t* empty_pw = full_pw + GEMM_PSTAGES;      // [PSTAGES] GM_REF4: W unpacked
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + GEMM_NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -226,7 +260,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // W producer's expect_tx arrival + (byte A) the A producer's expect_tx
       // arrival or (packed A) 2 unpacker arrivals (+ the peer's relay on the
       // leader)
-      mbar_init(&full_s[i], (BYTEA ? 2 : 3) + (leader ? 1 : 0));
+      // (GM_REF4: 2 A unpacker + 16 W unpacker arrivals, no copy into the stage)
+      mbar_init(&full_s[i], (PW ? 2 + GEMM_EPI_WARPS : BYTEA ? 2 : 3) + (leader ? 1 : 0));
       mbar_init(&empty_s[i], 1);
     }
     for (int i = 0; i < GEMM_PSTAGES; ++i) {
@@ -240,6 +275,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tmem_full[i], 1);
       mbar_init(&tmem_empty[i], 2 * GEMM_EPI_WARPS);
+    }
+    for (int i = 0; i < GEMM_PSTAGES; ++i) {
+      mbar_init(&full_pw[i], 1);
+      mbar_init(&empty_pw[i], GEMM_EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -266,18 +305,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int g = 0; g < G; ++g) {
           const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
           const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
-          if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&full_s[s], GEMM_W_BYTES);
-          // this CTA's 128 of the pair's 256 B columns (SwiGLU: gate | up)
-          tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_s[s], g * 128, wrow);
-          issued_w = g + 1;
+          if (PW) {
+            // packed W rows of this CTA into the packed-W stage (the epilogue
+            // warps unpack them into the stage the MMA reads)
+            if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pw[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+            mbar_arrive_expect_tx(&full_pw[ps], GEMM_PW_BYTES);
+            tma_load_2d(smem + GEMM_OFF_SC + ps * GEMM_PW_BYTES, wmap, &full_pw[ps], g * 64, wrow);
+            issued_w = g + 1;
+          } else {
+            if (g >= GEMM_STAGES && !mbar_wait(&empty_s[s], ph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+            mbar_arrive_expect_tx(&full_s[s], GEMM_W_BYTES);
+            // this CTA's 128 of the pair's 256 B columns (SwiGLU: gate | up)
+            tma_load_2d(smem + GEMM_OFF_W + s * GEMM_W_BYTES, wmap, &full_s[s], g * 128, wrow);
+            issued_w = g + 1;
+          }
           if (BYTEA) continue;  // A comes from the A producer (warp 2)
           if (g >= GEMM_PSTAGES && !mbar_wait(&empty_pa[ps], pph ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
           mbar_arrive_expect_tx(&full_pa[ps], GEMM_PA_BYTES);
           tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
           issued_pa = g + 1;
         }
-      } else if (lane == 1) {
+      } else if (lane == 1 && !REF) {
         // ------------------------------------------ W-scale chunk producer
         // Chunk c (groups kScGroups*c ..) goes to buffer c % 2 once the
         // epilogue has released chunk c - 2.  A thread of its own: copies
@@ -306,13 +354,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else if (warp == 1) {
       // ------------------------------------- MMA issuer (leader) / relay (peer)
       if (lane == 0 && leader) {
-        // fp32 accumulators, e4m3 x e4m3, both K-major
-        constexpr uint32_t idesc = make_idesc(1, 0, 0, 0, 0, 2 * GEMM_BM, GEMM_BN);
+        // fp32 accumulators of e4m3 (or fp8 formats of p.f8fmt) operands, or
+        // int32 of int8 operands (GM_REF8); both K-major
+        const uint32_t idesc = MODE == GM_REF8    ? make_idesc(2, 1, 1, 0, 0, 2 * GEMM_BM, GEMM_BN)
+                               : MODE == GM_REFF8 ? make_idesc(1, p.f8fmt & 7, (p.f8fmt >> 3) & 7, 0, 0,
+                                                               2 * GEMM_BM, GEMM_BN)
+                                                  : make_idesc(1, 0, 0, 0, 0, 2 * GEMM_BM, GEMM_BN);
         for (int g = 0; g < G; ++g) {
-          const int s = g % GEMM_STAGES, b = g & 1;
+          // reference contract: one accumulator over all of K in buffer 0
+          const int s = g % GEMM_STAGES, b = REF ? 0 : (g & 1);
           const uint32_t ph = (g / GEMM_STAGES) & 1, bph = (g >> 1) & 1;
-          if (!mbar_wait_cluster(&full_s[s], ph, abort_flag, ERR_WAIT_MMA)) break;
-          if (g >= 2 && !mbar_wait_cluster(&tmem_empty[b], bph ^ 1, abort_flag, ERR_WAIT_MMA)) break;
+          if (!mbar_wait_cluster(&full_s[s], ph, abort_flag, ERR_WAIT_MMA)) {
+            if (REF && issued_mma > 0) mma_commit_pair(&tmem_full[0]);  // for the teardown drain
+            break;
+          }
+          if (!REF && g >= 2 && !mbar_wait_cluster(&tmem_empty[b], bph ^ 1, abort_flag, ERR_WAIT_MMA)) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES);
           const uint32_t w_base = smem_u32(smem + GEMM_OFF_W + s * GEMM_W_BYTES);
@@ -320,10 +376,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = umma_desc_sw128(a_base + 32 * k, 16, 1024);
             const uint64_t bd = umma_desc_sw128(w_base + 32 * k, 16, 1024);
-            mma_f8_pair(tmem + b * GEMM_BN, ad, bd, idesc, k > 0 ? 1u : 0u);
+            const uint32_t acc = (k > 0 || (REF && g > 0)) ? 1u : 0u;
+            if (MODE == GM_REF8) mma_i8_pair(tmem + b * GEMM_BN, ad, bd, idesc, acc);
+            else mma_f8_pair(tmem + b * GEMM_BN, ad, bd, idesc, acc);
           }
           mma_commit_pair(&empty_s[s]);
-          mma_commit_pair(&tmem_full[b]);
+          if (!REF || g == G - 1) mma_commit_pair(&tmem_full[b]);
           issued_mma = g + 1;
         }
       } else if (lane == 0) {
@@ -434,64 +492,128 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         acc2[(slot0 + i) / 2 + 1] = __ffma2_rn(u1, make_float2(sw.z, sw.w), acc2[(slot0 + i) / 2 + 1]);
       }
     };
-    const uint32_t tcol = lane_base + ca;  // this thread's first column in buffer 0
-    uint32_t va[16], vb[16];
-    ok = mbar_wait_s(s_full_sc, 0, s_abort, ERR_WAIT_EPILOGUE) && mbar_wait_s(s_tfull, 0, s_abort, ERR_WAIT_EPILOGUE);
-    if (ok) {
-      tc_fence_after();
-      tmem_ld16(tcol, va);
-    }
-    __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
-    for (int g = 0; g < G && ok; ++g) {
-      const int b = g & 1, cbuf = (g / kScGroups) & 1;
-      const float sa = row_ok ? __half2float(sa_next) : 0.0f;
-      if (g + 1 < G) sa_next = sa_row[g + 1];
-      const float2 sa2 = make_float2(sa, sa);
-      const uint32_t scs = s_scales + cbuf * GEMM_SC_BYTES + (g % kScGroups) * GEMM_BN * 4;
-      const uint32_t taddr = tcol + b * GEMM_BN;
-      tmem_wait_ld_regs(va);
-      tmem_ld16(taddr + 16, vb);
-      dequant16(va, scs, 0, sa2);
-      tmem_wait_ld_regs(vb);
-      tmem_ld16(taddr + kCd, va);
-      dequant16(vb, scs + 64, 16, sa2);
-      tmem_wait_ld_regs(va);
-      tmem_ld16(taddr + kCd + 16, vb);
-      dequant16(va, scs + 4 * kCd, 32, sa2);
-      tmem_wait_ld_regs(vb);
-      // every column of group g is in registers: hand the buffer back to the MMA
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (leader) mbar_arrive_s(s_tempty + 8u * (uint32_t)b);
-        else mbar_arrive_remote(tmem_empty_remote + 8u * (uint32_t)b);
-      }
-      if (g + 1 < G) {
-        const int g1 = g + 1;
-        const int c1 = g1 / kScGroups;
-        if ((g1 % kScGroups != 0 ||
-             mbar_wait_s(s_full_sc + 8u * (uint32_t)(c1 & 1), (c1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) &&
-            mbar_wait_s(s_tfull + 8u * (uint32_t)(g1 & 1), (g1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) {
-          tc_fence_after();
-          tmem_ld16(tcol + (g1 & 1) * GEMM_BN, va);
-        } else {
-          ok = false;
+    float acc[64];
+    if constexpr (REF) {
+      if constexpr (PW) {
+        // Until the last group the epilogue warps unpack this CTA's packed W
+        // rows (one 16-byte chunk = 32 codes per thread and group) into the
+        // stage the MMA reads, in the A unpackers' layout.
+        const int t = threadIdx.x - 128;  // 0..511: row t/4, 32-column piece t%4
+        const int c = t & 3, r0 = t >> 2;
+        for (int g = 0; g < G && ok; ++g) {
+          const int s = g % GEMM_STAGES, ps = g % GEMM_PSTAGES;
+          const uint32_t ph = (g / GEMM_STAGES) & 1, pph = (g / GEMM_PSTAGES) & 1;
+          if (!mbar_wait_s(smem_u32(&full_pw[ps]), pph, s_abort, ERR_WAIT_EPILOGUE) ||
+              (g >= GEMM_STAGES && !mbar_wait_s(smem_u32(&empty_s[s]), ph ^ 1, s_abort, ERR_WAIT_EPILOGUE))) {
+            ok = false;
+            break;
+          }
+          const uint4 v = reinterpret_cast<const uint4*>(smem + GEMM_OFF_SC + ps * GEMM_PW_BYTES)[t];
+          uint4 lo, hi;
+          unpack_chunk(v, lo, hi);
+          uint8_t* dst = smem + GEMM_OFF_W + s * GEMM_W_BYTES + r0 * 128;
+          *reinterpret_cast<uint4*>(dst + (((2 * c) ^ (r0 & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ (r0 & 7)) << 4)) = hi;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&empty_pw[ps]);
+            mbar_arrive(&full_s[s]);
+          }
         }
       }
-      dequant16(vb, scs + 4 * kCd + 64, 48, sa2);
-      __syncwarp();
-      if (lane == 0 && (g % kScGroups == kScGroups - 1 || g == G - 1))
-        mbar_arrive_s(s_empty_sc + 8u * (uint32_t)cbuf);
-    }
-    if (!ok) tmem_wait_ld();  // no TMEM load stays in flight
-
-    float acc[64];
+      // One accumulator over all of K: p = fp32(fp32(acc * xs[r]) * ws[c])
+      // (+ bias[c]), the reference's projected() before its rounding to T.
+      ok = ok && mbar_wait_s(s_tfull, 0, s_abort, ERR_WAIT_EPILOGUE);
+      if (ok) {
+        tc_fence_after();
+        constexpr int kCd = pairw ? GEMM_BN / 2 : 32;
+        const uint32_t tcol = lane_base + ca;
+        uint32_t v[4][16];
+        tmem_ld16(tcol, v[0]);
+        tmem_ld16(tcol + 16, v[1]);
+        tmem_ld16(tcol + kCd, v[2]);
+        tmem_ld16(tcol + kCd + 16, v[3]);
+        tmem_wait_ld_regs(v[0]);
+        tmem_wait_ld_regs(v[1]);
+        tmem_wait_ld_regs(v[2]);
+        tmem_wait_ld_regs(v[3]);
+        const float xs = row_ok ? p.xs[(int64_t)row * p.xs_stride] : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      acc[2 * j] = acc2[j].x;
-      acc[2 * j + 1] = acc2[j].y;
-    }
+        for (int j = 0; j < 64; ++j) {
+          // register slot j: chunk j/16 of this thread's columns
+          const int cc = (j < 32 ? j : j - 32 + kCd);  // column within the tile, from ca
+          const int col = n0 + ca + cc;                // SwiGLU: gate (j < 32) / up (j >= 32) weight row
+          const bool up = pairw && j >= 32;
+          const int wcol = up ? n0 + ca + (j - 32) : (pairw ? n0 + ca + j : col);
+          const float* wsp = up ? S.wscale2 : S.wscale;
+          const bool cok = pairw || col < S.n;
+          const uint32_t raw = v[j >> 4][j & 15];
+          const float a = MODE == GM_REF8 ? __int2float_rn((int)raw) : __uint_as_float(raw);
+          float pv = cok ? __fmul_rn(__fmul_rn(a, xs), wsp[(int64_t)wcol * p.ws_stride]) : 0.0f;
+          if (p.bias && cok && !pairw) pv = __fadd_rn(pv, p.bias[col]);
+          acc[j] = pv;
+        }
+      }
+    } else {
+      const uint32_t tcol = lane_base + ca;  // this thread's first column in buffer 0
+      uint32_t va[16], vb[16];
+      ok = mbar_wait_s(s_full_sc, 0, s_abort, ERR_WAIT_EPILOGUE) && mbar_wait_s(s_tfull, 0, s_abort, ERR_WAIT_EPILOGUE);
+      if (ok) {
+        tc_fence_after();
+        tmem_ld16(tcol, va);
+      }
+      __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
+      for (int g = 0; g < G && ok; ++g) {
+        const int b = g & 1, cbuf = (g / kScGroups) & 1;
+        const float sa = row_ok ? __half2float(sa_next) : 0.0f;
+        if (g + 1 < G) sa_next = sa_row[g + 1];
+        const float2 sa2 = make_float2(sa, sa);
+        const uint32_t scs = s_scales + cbuf * GEMM_SC_BYTES + (g % kScGroups) * GEMM_BN * 4;
+        const uint32_t taddr = tcol + b * GEMM_BN;
+        tmem_wait_ld_regs(va);
+        tmem_ld16(taddr + 16, vb);
+        dequant16(va, scs, 0, sa2);
+        tmem_wait_ld_regs(vb);
+        tmem_ld16(taddr + kCd, va);
+        dequant16(vb, scs + 64, 16, sa2);
+        tmem_wait_ld_regs(va);
+        tmem_ld16(taddr + kCd + 16, vb);
+        dequant16(va, scs + 4 * kCd, 32, sa2);
+        tmem_wait_ld_regs(vb);
+        // every column of group g is in registers: hand the buffer back to the MMA
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive_s(s_tempty + 8u * (uint32_t)b);
+          else mbar_arrive_remote(tmem_empty_remote + 8u * (uint32_t)b);
+        }
+        if (g + 1 < G) {
+          const int g1 = g + 1;
+          const int c1 = g1 / kScGroups;
+          if ((g1 % kScGroups != 0 ||
+               mbar_wait_s(s_full_sc + 8u * (uint32_t)(c1 & 1), (c1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) &&
+              mbar_wait_s(s_tfull + 8u * (uint32_t)(g1 & 1), (g1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) {
+            tc_fence_after();
+            tmem_ld16(tcol + (g1 & 1) * GEMM_BN, va);
+          } else {
+            ok = false;
+          }
+        }
+        dequant16(vb, scs + 4 * kCd + 64, 48, sa2);
+        __syncwarp();
+        if (lane == 0 && (g % kScGroups == kScGroups - 1 || g == G - 1))
+          mbar_arrive_s(s_empty_sc + 8u * (uint32_t)cbuf);
+      }
+      if (!ok) tmem_wait_ld();  // no TMEM load stays in flight
 
+  #pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        acc[2 * j] = acc2[j].x;
+        acc[2 * j + 1] = acc2[j].y;
+      }
+
+    }
     // ---------------------------------------------------- final epilogue
     // CTA-uniform decision: every epilogue warp reaches this barrier, then all
     // of them see the same abort flag (the pair-exchanging paths have more).
@@ -711,8 +833,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 0 && lane == 0) {
       // (a stage's full barrier also waits for unpacker arrivals, so only
       // the transaction bytes are certain: drain with a bounded wait)
-      for (int g = (issued_w > GEMM_STAGES ? issued_w - GEMM_STAGES : 0); g < issued_w; ++g)
-        mbar_drain(&full_s[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
+      if (!PW)
+        for (int g = (issued_w > GEMM_STAGES ? issued_w - GEMM_STAGES : 0); g < issued_w; ++g)
+          mbar_drain(&full_s[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
       for (int g = (issued_pa > GEMM_PSTAGES ? issued_pa - GEMM_PSTAGES : 0); g < issued_pa; ++g)
         mbar_drain(&full_pa[g % GEMM_PSTAGES], (g / GEMM_PSTAGES) & 1);
     }
@@ -724,8 +847,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         mbar_drain(&full_sc[c & 1], (c >> 1) & 1);
     if (warp == 1 && lane == 0 && issued_mma > 0) {
       const int g = issued_mma - 1;
-      mbar_drain(&tmem_full[g & 1], (g >> 1) & 1);
+      if (REF) mbar_drain(&tmem_full[0], 0);
+      else mbar_drain(&tmem_full[g & 1], (g >> 1) & 1);
     }
+    if (PW && warp == 0 && lane == 0)
+      for (int g = (issued_w > GEMM_PSTAGES ? issued_w - GEMM_PSTAGES : 0); g < issued_w; ++g)
+        mbar_drain(&full_pw[g % GEMM_PSTAGES], (g / GEMM_PSTAGES) & 1);
   }
   tc_fence_before();
   __syncthreads();

@@ -17,6 +17,7 @@
 #include "k2b_common.cuh"
 #include "elementwise.cuh"
 #include "norm_quant.cuh"
+#include "ref_contract.cuh"
 
 #define K2B_EXPORT extern "C" __attribute__((visibility("default")))
 
@@ -147,13 +148,28 @@ struct SegDesc {
   const void* wscale2;    // SwiGLU: fp32 [K/128, n]
 };
 
-// bytea: `a` is e4m3 bytes [M, K] (the block loop's activation containers)
-// instead of packed INT4 [M, K/2].
+// Reference-contract arguments of gemm_launch (GM_REF* modes): activation
+// scales xs[r * xs_stride] and weight scales wscale[c * ws_stride] (fp32),
+// optional fp32 bias [n] (SEG_BF16), fp8 formats a | b << 3.
+struct RefScales {
+  const float* xs = nullptr;
+  int xs_stride = 1, ws_stride = 1;
+  const float* bias = nullptr;
+  uint32_t f8fmt = 0;
+};
+
+// mode (GemmMode): GM_PACKED `a` packed INT4 [M, K/2]; GM_BYTES e4m3 bytes
+// [M, K] (the block loop's activation containers); GM_REF4 packed INT4 A and
+// W with per-row / per-channel fp32 scales; GM_REF8 int8 A and W bytes;
+// GM_REFF8 fp8 A and W bytes.
 static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDesc* segs, int nseg, int length,
                        const float* freqs, const void* gate, const void* resid, cudaStream_t st,
-                       void* const* peers = nullptr, int tp = 0, int rank = 0, int chunk = 0, bool bytea = false) {
+                       void* const* peers = nullptr, int tp = 0, int rank = 0, int chunk = 0, int mode = GM_PACKED,
+                       const RefScales* ref = nullptr) {
+  const bool refm = mode >= GM_REF4;
+  const bool bytea = mode == GM_BYTES || mode == GM_REF8 || mode == GM_REFF8;
   if (M <= 0 || K <= 0 || K % 128 || nseg < 1 || nseg > 4 || length <= 0) return (int)cudaErrorInvalidValue;
-  if (!aligned16(a) || !sa) return (int)cudaErrorInvalidValue;
+  if (!aligned16(a) || (refm ? (!ref || !ref->xs) : !sa)) return (int)cudaErrorInvalidValue;
   CUtensorMap amap;
   WeightMaps wm;
   memset(&wm, 0, sizeof(wm));
@@ -167,15 +183,21 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     // SwiGLU pairs 128 gate + 128 up columns per tile; other segments take
     // any multiple of 128 columns (a last tile may be half used)
     const int tile_n = pairw ? GEMM_BN / 2 : GEMM_BN;
-    if (d.n <= 0 || d.n % 128 || !aligned16(d.w) || !aligned16(d.wscale) || !d.out) return (int)cudaErrorInvalidValue;
-    // each CTA of a pair loads 128 weight rows per K group
-    int rc = make_map_2d(&wm.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w, (uint64_t)K, (uint64_t)d.n, (uint64_t)K,
-                         128, GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (d.n <= 0 || d.n % 128 || !aligned16(d.w) || (refm ? !d.wscale : !aligned16(d.wscale)) || !d.out)
+      return (int)cudaErrorInvalidValue;
+    // each CTA of a pair loads 128 weight rows per K group: prepared / byte
+    // weights in the UMMA layout, or (GM_REF4) the packed rows as stored
+    auto wmap = [&](CUtensorMap* m, const void* w) {
+      return mode == GM_REF4 ? make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)K / 2, (uint64_t)d.n,
+                                           (uint64_t)K / 2, 64, GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE)
+                             : make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)K, (uint64_t)d.n,
+                                           (uint64_t)K, 128, GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+    };
+    int rc = wmap(&wm.m[i], d.w);
     if (rc) return rc;
     if (pairw) {
-      if (!aligned16(d.w2) || !aligned16(d.wscale2)) return (int)cudaErrorInvalidValue;
-      rc = make_map_2d(&wm.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d.w2, (uint64_t)K, (uint64_t)d.n, (uint64_t)K, 128,
-                       GEMM_BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (!aligned16(d.w2) || (refm ? !d.wscale2 : !aligned16(d.wscale2))) return (int)cudaErrorInvalidValue;
+      rc = wmap(&wm.m[1], d.w2);
       if (rc) return rc;
     }
     GemmSegment& g = p.seg[i];
@@ -215,6 +237,13 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
   p.freqs = freqs;
   p.gate = static_cast<const __nv_bfloat16*>(gate);
   p.resid = static_cast<const __nv_bfloat16*>(resid);
+  if (refm) {
+    p.xs = ref->xs;
+    p.xs_stride = ref->xs_stride;
+    p.ws_stride = ref->ws_stride;
+    p.bias = ref->bias;
+    p.f8fmt = ref->f8fmt;
+  }
   if (segs[0].kind == SEG_F32_SCATTER) {
     // rows 0..M-1 go to ranks row / chunk, all of which must exist
     if (nseg != 1 || !peers || tp < 1 || tp > 4 || rank < 0 || rank >= tp || chunk <= 0 ||
@@ -228,11 +257,17 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     p.scatter_rank = rank;
   }
   const bool pairw = segs[0].kind == SEG_SWIGLU || segs[0].kind == SEG_SWIGLU_BF16 || segs[0].kind == SEG_SWIGLU_E4M3;
-  void (*kern)(CUtensorMap, WeightMaps, GemmParams) =
-      pairw ? (bytea ? gemm_w4a4_kernel<true, true> : gemm_w4a4_kernel<true, false>)
-            : (bytea ? gemm_w4a4_kernel<false, true> : gemm_w4a4_kernel<false, false>);
-  const int variant = (pairw ? 1 : 0) + (bytea ? 2 : 0);
-  static bool attr_set[64][4] = {};
+  typedef void (*GemmKernel)(CUtensorMap, WeightMaps, GemmParams);
+  static const GemmKernel kernels[5][2] = {
+      {gemm_w4a4_kernel<false, GM_PACKED>, gemm_w4a4_kernel<true, GM_PACKED>},
+      {gemm_w4a4_kernel<false, GM_BYTES>, gemm_w4a4_kernel<true, GM_BYTES>},
+      {gemm_w4a4_kernel<false, GM_REF4>, gemm_w4a4_kernel<true, GM_REF4>},
+      {gemm_w4a4_kernel<false, GM_REF8>, nullptr},
+      {gemm_w4a4_kernel<false, GM_REFF8>, nullptr}};
+  if (mode < 0 || mode > GM_REFF8 || !kernels[mode][pairw ? 1 : 0]) return (int)cudaErrorInvalidValue;
+  GemmKernel kern = kernels[mode][pairw ? 1 : 0];
+  const int variant = 2 * mode + (pairw ? 1 : 0);
+  static bool attr_set[64][10] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
@@ -619,7 +654,7 @@ K2B_EXPORT int k2b_attention_quant_e4m3(const void* q, const void* k, const void
 K2B_EXPORT int k2b_gemm_f32_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, void* out, int m,
                                  int n, int k, void* stream) {
   SegDesc d = {SEG_F32, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
-  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, true);
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
 }
 
 K2B_EXPORT int k2b_qkv_e4m3(const void* a8, const void* sa, const void* wq, const void* swq, const void* wk,
@@ -635,7 +670,7 @@ K2B_EXPORT int k2b_qkv_e4m3(const void* a8, const void* sa, const void* wq, cons
   };
   const int nseg = (wg && go) ? 4 : 3;
   return gemm_launch(a8, sa, m, k, d, nseg, length, static_cast<const float*>(freqs), nullptr, nullptr,
-                     (cudaStream_t)stream, nullptr, 0, 0, 0, true);
+                     (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
 }
 
 K2B_EXPORT int k2b_gated_residual_e4m3(const void* a8, const void* sa, const void* w, const void* wscale,
@@ -643,14 +678,14 @@ K2B_EXPORT int k2b_gated_residual_e4m3(const void* a8, const void* sa, const voi
                                        int k, void* stream) {
   SegDesc d = {SEG_RESIDUAL, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
   return gemm_launch(a8, sa, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0, 0,
-                     true);
+                     GM_BYTES);
 }
 
 K2B_EXPORT int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
                                      const void* su, void* h8, void* hs, int m, int width, int k, void* stream) {
   if (width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
   SegDesc d = {SEG_SWIGLU_E4M3, width, wg, sg, h8, width, nullptr, 0.0f, hs, wu, su};
-  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, true);
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
 }
 
 #include "abi_reference.cuh"

@@ -59,6 +59,10 @@ SIGNATURES = {
     "k2_elementwise": (None, [_P] * 4 + [ctypes.c_int64, _I, _I, _I, _P]),
     "k2_rope": (None, [_P] * 5 + [_I] * 7 + [_P]),
     "k2b_shim_status": (_I, [_I]),
+    "k2_quant8": (None, [_P] * 3 + [ctypes.c_int64] * 2 + [_I, _I, _P]),
+    "k2_gemm4": (None, [_P] * 6 + [ctypes.c_int64] * 3 + [_I, _P]),
+    "k2_dequant8": (None, [_P] * 5 + [ctypes.c_int64] * 3 + [_I, _P]),
+    "k2_fp8": (None, [_P, _P, _P, ctypes.c_int64, _I, _I, ctypes.c_bool, _P]),
     "k2b_norm_quant_e4m3": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
     "k2b_attention_quant_e4m3": (_I, [_P] * 5 + [_I] * 6 + [_LL] * 9 + [_P]),
     "k2b_gemm_f32_e4m3": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),

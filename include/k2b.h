@@ -28,6 +28,7 @@
 #ifndef K2B_H
 #define K2B_H
 
+#include <stdbool.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -267,12 +268,21 @@ int k2b_forward_blocks_static(const void* const* block_ptrs, int nblocks, void* 
                               int length, int hidden, int heads, int kvheads, int mlp, float eps, float qk_eps,
                               void* stream);
 
-/* -------------------------------------- reference-named exports (shims) --
- * Same names and argument order as the reference's kernel libraries so that
- * native_runtime.cpp's configure()/configure_joint()/configure_norm_quant()
- * dlsym calls resolve unchanged; data follows the contract above.
- * group must be 128 and dtype 2 (bf16) for k2_norm_mod_quant4; dtype 0
- * (bf16) for the k2_int4_* family; batch 1 (length = m). */
+/* ------------------------------- reference-named exports (reference contract) --
+ * The symbols the reference's runtime dlsym's (configure(): k2_quant4,
+ * k2_quant8, k2_gemm4, k2_dequant8, k2_fp8, k2_norm, k2_elementwise, k2_rope;
+ * the epilogue/QK libraries: k2_int4_gated_residual, k2_int4_qk_norm_rope;
+ * configure_joint(): k2_int4_swiglu, k2_int4_qkv, k2_int4_residual_norm;
+ * configure_norm_quant(): k2_norm_mod_quant4; native_runtime.cpp:514-529),
+ * with the reference's argument order AND its data contract, i.e. the
+ * buffers native_runtime.cpp allocates for them (:262-311, 399-447):
+ *   - INT4 activations packed [m, k/2] + ONE fp32 scale per row [m, 1],
+ *     ConvRot-rotated in groups of 16, 64 or 256;
+ *   - INT4 weights packed [n, k/2] as stored by a ConvRot W4A4 checkpoint,
+ *     one fp32 scale per channel [n] (nothing prepared ahead);
+ *   - projections T(fp32(fp32(acc*xs[r])*ws[c])), acc over all of k;
+ *   - dtype 0 = bf16 for k2_int4_*, 2 = bf16 for the others; fp16 rejected.
+ * The group-128 BASELINE contract is served by the k2b_* entry points only. */
 int k2_norm_mod_quant4(const void* x, const void* norm, const void* scale, const void* shift, void* q, void* scales,
                        int rows, int K, int length, int cut, int batch, float eps, int group, int dtype,
                        void* stream); /* kernels/norm_quant.cu:89-91 */
@@ -286,20 +296,32 @@ int k2_int4_gated_residual(void* a, void* w, void* xs, void* ws, void* gate, voi
                            int n, int k, int dtype, int config, void* stream); /* kernels/int4_epilogue.cu:77-78 */
 int k2_int4_qk_norm_rope(void* a, void* w, void* xs, void* ws, void* norm, void* freqs, void* output, int m, int n,
                          int k, int dtype, float eps, void* stream); /* kernels/qk_norm_rope.cu:135 */
-
 int k2_int4_residual_norm(void* a, void* w, void* xs, void* ws, void* gate, void* residual, void* norm, void* scale,
                           void* shift, void* output, void* normalized, void* counters, int m, int n, int k, int dtype,
                           float eps, void* stream); /* kernels/joint_projection.cu:212-214 */
-/* The reference's void exports (kernels/native_dispatch.cu:23-29, 79-95):
+/* The reference's void exports (kernels/native_dispatch.cu:23-40, 79-95):
  * unsupported input launches nothing and sets the status k2b_shim_status()
- * returns (bf16 = dtype 2 only; k2_quant4: group 128, fp16 group scales). */
+ * returns.  k2_quant4 / k2_quant8: q [m, k/2] INT4 / [m, k] int8, s fp32
+ * [m, 1] (group 16/64/256, k2_quant8 also 0 = no rotation); k2_gemm4: bias
+ * fp32 [n] or null, out bf16 [m, n]; k2_dequant8: int32 a [m, n] -> bf16,
+ * ws [ns] with ns = n or 1, bias bf16 [n] or null; k2_fp8: y = fp8(x / s[0])
+ * (quant) or T(x * s[0]), codes 0 fp32 / 1 fp16 / 2 bf16 / 5 e4m3 / 6 e5m2. */
 void k2_norm(const void* x, const void* w, const void* scale, const void* shift, void* y, int rows, int d, int length,
-             int cut, int batch, float eps, int dtype, void* stream);
-void k2_quant4(const void* x, void* q, void* s, int64_t m, int64_t k, int group, int dtype, void* stream);
+             int cut, int batch, float eps, int dtype, void* stream); /* kernels/native_dispatch.cu:79-83 */
+void k2_quant4(const void* x, void* q, void* s, int64_t m, int64_t k, int group, int dtype,
+               void* stream); /* kernels/native_dispatch.cu:23-25 */
+void k2_quant8(const void* x, void* q, void* s, int64_t m, int64_t k, int group, int dtype,
+               void* stream); /* kernels/native_dispatch.cu:30-33 */
+void k2_gemm4(const void* a, const void* w, const void* xs, const void* ws, const void* bias, void* out, int64_t m,
+              int64_t n, int64_t k, int dtype, void* stream); /* kernels/native_dispatch.cu:26-29 */
+void k2_dequant8(const void* a, const void* xs, const void* ws, const void* bias, void* out, int64_t m, int64_t n,
+                 int64_t ns, int dtype, void* stream); /* kernels/native_dispatch.cu:34-36 */
+void k2_fp8(const void* x, void* y, const void* s, int64_t n, int src, int dst, bool quant,
+            void* stream); /* kernels/native_dispatch.cu:37-40 */
 void k2_elementwise(const void* a, const void* b, const void* r, void* y, int64_t n, int mode, int width, int dtype,
-                    void* stream);
+                    void* stream); /* kernels/native_dispatch.cu:84-89 */
 void k2_rope(const void* q, const void* k, const void* f, void* qo, void* ko, int batch, int length, int qh, int kh,
-             int dim, int fb, int dtype, void* stream);
+             int dim, int fb, int dtype, void* stream); /* kernels/native_dispatch.cu:90-95 */
 /* Last non-zero status of a void shim on this host thread; reset clears it.
  * No counterpart in the reference (its void exports rely on
  * cudaGetLastError()). */

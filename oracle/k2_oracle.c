@@ -476,3 +476,76 @@ void k2o_exp_vec(const float* x, float* y, int64_t n) {
 void k2o_bf16_round_vec(const float* x, uint16_t* y, int64_t n) {
     for (int64_t i = 0; i < n; ++i) y[i] = k2o_f32_to_bf16(x[i]);
 }
+
+/* ------------------------------------------- reference contract (parity) */
+
+/* The reference runtime's INT4 / int8 activation quantisation (its own data
+ * contract, native_runtime.cpp:262-271, 432-447), as the library's
+ * reference-named exports compute it (csrc/ref_contract.cuh):
+ *   optional RMSNorm + modulation with the rounding points of k2o_norm_mod
+ *   (kernels/norm_quant.cu:20-38), bf16 values v;
+ *   ConvRot in groups of G = 16, 64 or 256 (0: none): radix-4 stages at
+ *   strides 1, 4, 16, 64 (kernels/norm_quant.cu:48-60 names the stages; the
+ *   stage arithmetic lives in comfy-kitchen, not in the reference, and is this
+ *   project's restatement): (a, b, c, d) -> bf16(((a+b)+(c+d))*0.5),
+ *   bf16(((a-b)+(c-d))*0.5), bf16(((a+b)-(c+d))*0.5), bf16(((a-b)-(c-d))*0.5);
+ *   scale = max(min(amax, bf16 max)/qmax, 1e-10) per row (qmax 7 or 127),
+ *   inverse = 1/scale, code = clamp(rne(v*inverse), -8|-127, 7|127)
+ *   (kernels/norm_quant.cu:61-66);
+ *   bits 4: two codes per byte, even column low; bits 8: int8 codes.
+ * x bf16 [rows, K]; w/scale/shift as k2o_norm_mod (w == NULL: no norm). */
+int k2o_ref_quant(const uint16_t* x, const float* w, const uint16_t* scale, const uint16_t* shift, uint8_t* q,
+                  float* s, int rows, int K, int length, int cut, int batch, float eps, int group, int bits) {
+    if (rows <= 0 || K <= 0 || K % 8 || (group != 0 && group != 16 && group != 64 && group != 256) ||
+        (group && K % group) || (bits != 4 && bits != 8))
+        return 1;
+    uint16_t* v = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)K);
+    const float qmax = bits == 4 ? 7.0f : 127.0f;
+    for (int r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + (int64_t)r * K;
+        if (w) {
+            /* one row through the norm/mod restatement, with the row's latent */
+            int b = r / length;
+            if (cut >= 0 && r % length >= cut) b += batch;
+            k2o_norm_mod(xr, w, scale ? scale + (int64_t)b * K : NULL, shift ? shift + (int64_t)b * K : NULL, v, 1,
+                         K, 1, -1, 1, eps);
+        } else {
+            memcpy(v, xr, sizeof(uint16_t) * (size_t)K);
+        }
+        for (int st = 1; group && st < group; st *= 4) {
+            for (int t = 0; t < K / 4; ++t) {
+                const int base = (t / st) * 4 * st + (t % st);
+                const float a = bf(v[base]), bb = bf(v[base + st]), c = bf(v[base + 2 * st]), d = bf(v[base + 3 * st]);
+                const float s01 = a + bb, d01 = a - bb, s23 = c + d, d23 = c - d;
+                v[base] = k2o_f32_to_bf16((s01 + s23) * 0.5f);
+                v[base + st] = k2o_f32_to_bf16((d01 + d23) * 0.5f);
+                v[base + 2 * st] = k2o_f32_to_bf16((s01 - s23) * 0.5f);
+                v[base + 3 * st] = k2o_f32_to_bf16((d01 - d23) * 0.5f);
+            }
+        }
+        float amax = 0.0f;
+        for (int c = 0; c < K; ++c) amax = fmaxf(amax, fabsf(bf(v[c])));
+        if (amax > 3.3895313892515355e38f) amax = 3.3895313892515355e38f;
+        float sc = amax / qmax;
+        if (sc < 1e-10f) sc = 1e-10f;
+        s[r] = sc;
+        const float inverse = 1.0f / sc;
+        if (bits == 4) {
+            uint8_t* qr = q + (int64_t)r * (K / 2);
+            for (int i = 0; i < K / 2; ++i) {
+                float c0 = rintf(bf(v[2 * i]) * inverse), c1 = rintf(bf(v[2 * i + 1]) * inverse);
+                c0 = fminf(fmaxf(c0, -8.0f), 7.0f);
+                c1 = fminf(fmaxf(c1, -8.0f), 7.0f);
+                qr[i] = (uint8_t)(((int)c0 & 0xF) | (((int)c1 & 0xF) << 4));
+            }
+        } else {
+            int8_t* qr = (int8_t*)q + (int64_t)r * K;
+            for (int i = 0; i < K; ++i) {
+                float c = rintf(bf(v[i]) * inverse);
+                qr[i] = (int8_t)(int)fminf(fmaxf(c, -127.0f), 127.0f);
+            }
+        }
+    }
+    free(v);
+    return 0;
+}

@@ -67,6 +67,7 @@ def _declare(L):
     L.k2o_unpack_weight.argtypes = [P, P, I, I, P, P]
     L.k2o_gemm_w4a4_cols.argtypes = [P, P, P, P, I, I, I, P, I, I, I, P, I, P]
     L.k2o_dequant_group.argtypes = [P, P, P, P, I, I]
+    L.k2o_ref_quant.argtypes = [P, P, P, P, P, P, I, I, I, I, I, F, I, I]
     L.k2o_qk_norm_rope.argtypes = [P, I, I, I, P, F, P, I, P, P]
     L.k2o_gated_residual.argtypes = [P, I, I, P, P, I, P, P]
     L.k2o_swiglu_quant.argtypes = [P, P, I, I, P, P, P]
@@ -418,3 +419,53 @@ def rope_table(pos: np.ndarray, axes, theta: float) -> np.ndarray:
         cos, sin = np.cos(angle), np.sin(angle)
         pieces.append(np.stack([cos, -sin, sin, cos], axis=-1).reshape(pos.shape[0], d // 2, 2, 2))
     return np.concatenate(pieces, axis=1).astype(np.float32)
+
+
+# ------------------------------------------------- reference contract (parity)
+# The reference's own data contract at its kernel-library symbols
+# (native_runtime.cpp:262-311, 399-447): one fp32 scale per activation row and
+# per weight channel, ConvRot in groups of 16/64/256, full-K accumulation.
+
+def ref_quant(x, w=None, scale=None, shift=None, length=None, cut=-1, batch=None, eps=1e-6, group=256, bits=4):
+    """x bf16 bits [rows, K] -> (q u8 [rows, K/2] packed INT4 or int8 [rows, K],
+    s fp32 [rows]); optional RMSNorm + modulation first (w fp32 "w+1" form,
+    scale/shift bf16 bits [nb, K]).  k2o_ref_quant."""
+    x = _c(x, np.uint16)
+    rows, K = x.shape
+    length = rows if length is None else length
+    batch = max(1, rows // length) if batch is None else batch
+    q = np.empty((rows, K // 2 if bits == 4 else K), np.uint8 if bits == 4 else np.int8)
+    s = np.empty(rows, np.float32)
+    wv = None if w is None else _c(w, np.float32)
+    sc = None if scale is None else _c(scale, np.uint16)
+    sh = None if shift is None else _c(shift, np.uint16)
+    assert lib().k2o_ref_quant(_p(x), _p(wv), _p(sc), _p(sh), _p(q), _p(s), rows, K, length, cut, batch,
+                               ctypes.c_float(eps), group, bits) == 0
+    return q, s
+
+
+def int4_codes(packed):
+    """packed u8 [rows, K/2] -> int8 codes [rows, K] (low nibble = even column)."""
+    p = _c(packed, np.uint8)
+    c = np.empty((p.shape[0], p.shape[1] * 2), np.int8)
+    lo, hi = (p & 0xF).astype(np.int8), (p >> 4).astype(np.int8)
+    c[:, 0::2] = np.where(lo >= 8, lo - 16, lo)
+    c[:, 1::2] = np.where(hi >= 8, hi - 16, hi)
+    return c
+
+
+def ref_project(a_codes, xs, w_codes, ws, bias=None):
+    """Reference-contract projection before its rounding to T:
+    p = fp32(fp32(float(acc) * xs[r]) * ws[c]) (+ bias[c]), acc over all of K
+    (kernels/joint_projection.cu:57-59).  a_codes [m, K], w_codes [n, K] integer
+    codes (INT4 or int8); the accumulators are exact integers (fp32 BLAS of
+    integer codes whose partial sums stay below 2^24 in magnitude)."""
+    a = np.asarray(a_codes, np.float32)
+    w = np.asarray(w_codes, np.float32)
+    acc = a @ w.T
+    assert np.abs(acc).max(initial=0) < 2 ** 24
+    p = (acc.astype(np.float32) * _c(xs, np.float32).reshape(-1, 1)).astype(np.float32)
+    p = (p * _c(ws, np.float32).reshape(1, -1)).astype(np.float32)
+    if bias is not None:
+        p = (p + _c(bias, np.float32).reshape(1, -1)).astype(np.float32)
+    return p

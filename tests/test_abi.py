@@ -74,3 +74,29 @@ def test_version_and_layout_queries(lib):
 def test_invalid_arguments_are_rejected_on_the_host(lib, call):
     """cudaErrorInvalidValue (1), returned before any launch (kernels/norm_quant.cu:92 convention)."""
     assert call(lib) == 1
+
+
+# Every symbol the reference's runtime resolves from its kernel libraries with
+# dlopen(RTLD_NOW | RTLD_LOCAL) + dlsym, each failing with "Missing native
+# symbol" (native_runtime.cpp:34-48): configure() (:514-521), configure_joint()
+# (:524-528), configure_norm_quant() (:529).
+REFERENCE_SYMBOLS = {
+    "configure: kernels": ["k2_quant4", "k2_quant8", "k2_gemm4", "k2_dequant8", "k2_fp8", "k2_norm",
+                           "k2_elementwise", "k2_rope"],
+    "configure: epilogue": ["k2_int4_gated_residual"],
+    "configure: qk": ["k2_int4_qk_norm_rope"],
+    "configure_joint": ["k2_int4_swiglu", "k2_int4_qkv", "k2_int4_residual_norm"],
+    "configure_norm_quant": ["k2_norm_mod_quant4"],
+}
+
+
+def test_reference_runtime_resolves_every_symbol():
+    """libk2b opened the way the reference's configure() opens its libraries
+    resolves every name each configure* call loads."""
+    import os
+
+    from k2b._native import LIB_PATH
+
+    h = ctypes.CDLL(LIB_PATH, mode=os.RTLD_NOW | os.RTLD_LOCAL)
+    missing = [n for names in REFERENCE_SYMBOLS.values() for n in names if not hasattr(h, n)]
+    assert not missing, missing

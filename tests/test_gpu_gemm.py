@@ -170,26 +170,3 @@ def test_swiglu_quant_bitexact(cuda, M, F, K):
     assert np.array_equal(bits(h), rh)
     assert np.array_equal(bits(hs), rs)
     assert np.array_equal(hq.cpu().numpy(), rq)
-
-
-def test_reference_named_qkv(cuda):
-    """k2_int4_qkv (kernels/joint_projection.cu:222) resolves and matches k2b_qkv."""
-    import torch
-    from k2b._native import lib
-
-    M, K, heads, kvheads = 256, 512, 2, 2
-    a, sa, ws, nq, nk, freqs, q, k, v, g = _qkv_case(cuda, M, M, heads, kvheads, K, gate=True, seed=4)
-    P = {n: _prep(cuda, *ws[n]) for n in ("q", "k", "v", "g")}
-    at, sat = t_u8(a, cuda), t_f16(sa, cuda)
-    nqt, nkt, ft = t_f32(nq, cuda), t_f32(nk, cuda), t_f32(freqs, cuda)
-    outs = [torch.empty_like(t) for t in (q, k, v, g)]
-    p = lambda t: ctypes.c_void_p(t.data_ptr())
-    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = lib().k2_int4_qkv(p(at), p(P["q"].w), p(P["k"].w), p(P["v"].w), p(P["g"].w), p(sat), p(P["q"].scale),
-                           p(P["k"].scale), p(P["v"].scale), p(P["g"].scale), p(nqt), p(nkt), p(ft),
-                           *[p(o) for o in outs], M, heads * 128, kvheads * 128, K, 0, ctypes.c_float(1e-6),
-                           ctypes.c_float(1e-5), st)
-    assert rc == 0
-    torch.cuda.synchronize()
-    for o, r in zip(outs, (q, k, v, g)):
-        assert torch.equal(o, r)

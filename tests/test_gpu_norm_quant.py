@@ -55,8 +55,12 @@ def test_rotate_quant_bitexact(cuda, rows, K):
     assert np.array_equal(bits(s), so) and np.array_equal(q.cpu().numpy(), qo)
 
 
-def test_reference_named_export(cuda):
-    """k2_norm_mod_quant4 (kernels/norm_quant.cu:89) with group 128 / bf16."""
+def test_reference_named_export_keeps_the_reference_contract(cuda):
+    """k2_norm_mod_quant4 (kernels/norm_quant.cu:89) writes ONE fp32 scale per
+    row into the reference's [rows, 1] buffer (group 256 here); group 128, which
+    the reference's own kernel rejects, is rejected, so a reference-sized scale
+    buffer can never receive group-128 scales.  (Bit-exactness of the contract:
+    tests/test_gpu_ref_contract.py.)"""
     import torch
     from k2b._native import lib
 
@@ -65,17 +69,16 @@ def test_reference_named_export(cuda):
     w, sc, sh = norm_inputs(K, 1, 22)
     x, wt, sct, sht = t_bf16(xb, cuda), t_f32(w, cuda), t_bf16(sc, cuda), t_bf16(sh, cuda)
     q = torch.empty((rows, K // 2), dtype=torch.uint8, device=cuda)
-    s = torch.empty((rows, K // 128), dtype=torch.float16, device=cuda)
+    s = torch.full((rows + 1, 1), -1.0, dtype=torch.float32, device=cuda)  # one guard row
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     P = lambda t: ctypes.c_void_p(t.data_ptr())
-    rc = lib().k2_norm_mod_quant4(P(x), P(wt), P(sct), P(sht), P(q), P(s), rows, K, rows, -1, 1,
-                                  ctypes.c_float(1e-6), 128, 2, st)
-    assert rc == 0
-    # unsupported group / dtype are rejected like kernels/norm_quant.cu:92
     assert lib().k2_norm_mod_quant4(P(x), P(wt), P(sct), P(sht), P(q), P(s), rows, K, rows, -1, 1,
-                                    ctypes.c_float(1e-6), 256, 2, st) != 0
-    assert lib().k2_norm_mod_quant4(P(x), P(wt), P(sct), P(sht), P(q), P(s), rows, K, rows, -1, 1,
-                                    ctypes.c_float(1e-6), 128, 1, st) != 0
+                                    ctypes.c_float(1e-6), 256, 2, st) == 0
+    for group, dtype in ((128, 2), (256, 1), (32, 2)):
+        assert lib().k2_norm_mod_quant4(P(x), P(wt), P(sct), P(sht), P(q), P(s), rows, K, rows, -1, 1,
+                                        ctypes.c_float(1e-6), group, dtype, st) != 0
     torch.cuda.synchronize()
-    qo, so = O.norm_quant(xb, w, sc, sh, eps=1e-6)
-    assert np.array_equal(bits(s), so) and np.array_equal(q.cpu().numpy(), qo)
+    sv = s.cpu().numpy()[:, 0]
+    assert (sv[:rows] > 0).all() and sv[rows] == -1.0  # nothing written past [rows, 1]
+    qo, so = O.ref_quant(xb, w, sc, sh, group=256)
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(sv[:rows], so)

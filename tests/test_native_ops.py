@@ -104,7 +104,7 @@ def test_void_shims_report_unsupported_input():
 
     L = lib()
     L.k2b_shim_status(1)
-    L.k2_quant4(None, None, None, 4, 512, 64, 2, None)          # group 64
+    L.k2_quant4(None, None, None, 4, 512, 128, 2, None)         # group 128 (not a reference group)
     assert L.k2b_shim_status(1) == 1                               # cudaErrorInvalidValue
     L.k2_norm(None, None, None, None, None, 4, 512, 4, -1, 1, ctypes.c_float(1e-6), 1, None)  # fp16
     assert L.k2b_shim_status(0) == 1 and L.k2b_shim_status(1) == 1 and L.k2b_shim_status(0) == 0
