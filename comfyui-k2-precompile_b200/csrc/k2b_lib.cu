@@ -688,5 +688,79 @@ K2B_EXPORT int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void*
   return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
 }
 
+// ------------------------------------------------ INT8 / FP8 weight formats
+// Projections of checkpoints stored as INT8 or FP8 weights (the reference's
+// formats 2 and 3/4, native_runtime.cpp:271-283, 298-311), on the same pair
+// GEMM with the whole of K in one accumulator and the dequant in the
+// epilogue: out = bf16(fp32(fp32(acc * xs[r * xs_stride]) * ws[c * ws_stride])
+// + bias[c]).  The reference runs at::_int_mm + k2_dequant8 (INT8) and
+// at::_scaled_mm (FP8) there.
+//   k2b_gemm8:  a8 int8 [m, k] (k2_quant8's rows), w8 int8 [n, k], int32
+//               accumulator;
+//   k2b_gemm_f8: a8 / w8 fp8 [m, k] / [n, k], fmt 0 e4m3 / 1 e5m2 each, fp32
+//               accumulator.
+// ws_stride / xs_stride 0: one scale for the whole operand.  bias fp32 [n] or
+// null.  k % 128 == 0, n % 128 == 0.
+K2B_EXPORT int k2b_gemm8(const void* a8, const void* xs, int xs_stride, const void* w8, const void* ws, int ws_stride,
+                         const void* bias, void* out, int m, int n, int k, void* stream) {
+  if ((xs_stride != 0 && xs_stride != 1) || (ws_stride != 0 && ws_stride != 1)) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_BF16, n, w8, ws, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  r.xs_stride = xs_stride;
+  r.ws_stride = ws_stride;
+  r.bias = static_cast<const float*>(bias);
+  return gemm_launch(a8, nullptr, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                     GM_REF8, &r);
+}
+
+K2B_EXPORT int k2b_gemm_f8(const void* a8, const void* xs, int xs_stride, const void* w8, const void* ws,
+                           int ws_stride, const void* bias, void* out, int m, int n, int k, int afmt, int bfmt,
+                           void* stream) {
+  if ((xs_stride != 0 && xs_stride != 1) || (ws_stride != 0 && ws_stride != 1) || (afmt != 0 && afmt != 1) ||
+      (bfmt != 0 && bfmt != 1))
+    return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_BF16, n, w8, ws, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  r.xs_stride = xs_stride;
+  r.ws_stride = ws_stride;
+  r.bias = static_cast<const float*>(bias);
+  r.f8fmt = (uint32_t)afmt | ((uint32_t)bfmt << 3);
+  return gemm_launch(a8, nullptr, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                     GM_REFF8, &r);
+}
+
+// Reference-contract INT4 joint QKV / SwiGLU / gated residual for a stream of
+// `batch` latents of `length` tokens (the reference-named exports take one
+// latent): RoPE token = row % length, gate row = row / length.
+K2B_EXPORT int k2b_ref_qkv(const void* a, const void* xs, const void* wq, const void* sq, const void* wk,
+                           const void* sk, const void* wv, const void* sv, const void* wg, const void* sg,
+                           const void* nq, const void* nk, const void* freq, void* qo, void* ko, void* vo, void* go,
+                           int m, int length, int qwidth, int kvwidth, int k, float eq, float ek, void* stream) {
+  if (qwidth <= 0 || kvwidth <= 0 || qwidth % 128 || kvwidth % 128 || length <= 0 || !freq)
+    return (int)cudaErrorInvalidValue;
+  SegDesc d[4] = {
+      {SEG_QKNORM, qwidth, wq, sq, qo, qwidth, static_cast<const float*>(nq), eq, nullptr, nullptr, nullptr},
+      {SEG_QKNORM, kvwidth, wk, sk, ko, kvwidth, static_cast<const float*>(nk), ek, nullptr, nullptr, nullptr},
+      {SEG_BF16, kvwidth, wv, sv, vo, kvwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+      {SEG_SIGMOID, qwidth, wg, sg, go, qwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+  };
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  return gemm_launch(a, nullptr, m, k, d, (wg && go) ? 4 : 3, length, static_cast<const float*>(freq), nullptr,
+                     nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_REF4, &r);
+}
+
+K2B_EXPORT int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const void* ws, const void* gate,
+                                      const void* residual, void* out, int m, int length, int n, int k,
+                                      void* stream) {
+  SegDesc d = {SEG_RESIDUAL, n, w, ws, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  return gemm_launch(a, nullptr, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0,
+                     0, GM_REF4, &r);
+}
+
 #include "abi_reference.cuh"
 #include "block_loop.cuh"

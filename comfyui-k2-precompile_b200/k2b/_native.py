@@ -60,6 +60,10 @@ SIGNATURES = {
     "k2_rope": (None, [_P] * 5 + [_I] * 7 + [_P]),
     "k2b_shim_status": (_I, [_I]),
     "k2_quant8": (None, [_P] * 3 + [ctypes.c_int64] * 2 + [_I, _I, _P]),
+    "k2b_gemm8": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _P]),
+    "k2b_gemm_f8": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "k2b_ref_qkv": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
+    "k2b_ref_gated_residual": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
     "k2_gemm4": (None, [_P] * 6 + [ctypes.c_int64] * 3 + [_I, _P]),
     "k2_dequant8": (None, [_P] * 5 + [ctypes.c_int64] * 3 + [_I, _P]),
     "k2_fp8": (None, [_P, _P, _P, ctypes.c_int64, _I, _I, ctypes.c_bool, _P]),

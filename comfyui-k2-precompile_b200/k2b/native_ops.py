@@ -9,13 +9,19 @@ reference registers in native_schedule.py:70-114 and input_quant_ops.py:34-42.
 
 Weights are referenced by integer keys through the same registry calls the
 reference's extension module exposes (``add_binding`` / ``release_bindings``,
-native_runtime.cpp:528, 573).  Registration converts an INT4 projection
-once into the GEMM's resident layout (weights are never streamed per call).
+native_runtime.cpp:528, 573).  A projection binding is served in one of two
+data contracts, chosen from what is registered:
 
-Data contract (the B200 build's, documented in the C header): packed
-activations are uint8 codes viewed as int8 [M, K/2] with fp16 group-128 scales
-[M, K/128] (the reference returns one fp32 scale per row); INT4 weights are
-registered as packed [N, K/2] + fp16 [N, K/128] group scales (``group`` 128).
+* the reference's own (``Binding.ref``): format 1 INT4 with ConvRot groups
+  16/64/256, packed [N, K/2] weights and fp32 per-channel scales [N]; format
+  2 INT8 [N, K]; formats 3/4 FP8 e4m3/e5m2 [N, K] with their scale; format 0
+  plain weights.  Activations are quantised per row with one fp32 scale
+  ([M, 1]) exactly as the reference's runtime quantises them
+  (native_runtime.cpp:266-285) and projected by the tcgen05 GEMM with the
+  whole of K in one accumulator (k2b.ref_ops);
+* group-128 W4A4 (``Binding.weight``): format 1, group 128 and fp16 group
+  scales [N, K/128]; converted once into the GEMM's resident layout; packed
+  activations carry fp16 group-128 scales [M, K/128].
 
 Only CUDA implementations are registered: a CPU tensor reaches no kernel and
 torch raises, there is no eager fallback.
@@ -29,11 +35,36 @@ from typing import Dict, List, Optional, Sequence
 
 import torch
 
-from . import ops
+from . import ops, ref_ops
 
 HEAD_DIM = 128
 
 # --------------------------------------------------------------- registry
+
+
+@dataclass
+class RefWeight:
+    """A projection kept in the checkpoint's own format (reference contract).
+
+    ``w``: int8 packed [np, kp/2] (format 1), int8 [np, kp] (format 2), fp8
+    [np, kp] (3/4) or the plain weight [n, k] (format 0), where np / kp are n
+    and k rounded up to the GEMM's 128 with zero rows / columns (zero codes
+    add nothing to an accumulator; padded output columns are dropped).
+    ``ws``: fp32 per-channel [np] or single [1] scale.  ``bias``: fp32 [np],
+    rounded the way the reference hands it to the kernel of this format."""
+
+    format: int
+    group: int
+    w: torch.Tensor
+    ws: Optional[torch.Tensor]
+    bias: Optional[torch.Tensor]
+    input_scale: Optional[torch.Tensor]
+    n: int
+    k: int
+
+    @property
+    def padded(self) -> bool:
+        return self.format != 0 and (self.n % 128 != 0 or self.k % 128 != 0)
 
 
 @dataclass
@@ -42,7 +73,7 @@ class Binding:
 
     key: int
     kind: int          # 0 projection, 1 RMSNorm, 2 RoPE table, 3/4 bias / modulation add
-    format: int        # 1: INT4 (the only projection format of this build)
+    format: int        # 0 plain, 1 INT4, 2 INT8, 3 FP8 e4m3, 4 FP8 e5m2
     group: int
     fuse: bool
     eps: float
@@ -50,6 +81,7 @@ class Binding:
     theta: float
     optimize_io: bool
     weight: Optional[ops.PreparedWeight] = None
+    ref: Optional[RefWeight] = None
     tensors: List[torch.Tensor] = field(default_factory=list)
     lookahead: List[int] = field(default_factory=list)
     routes: Dict[int, int] = field(default_factory=dict)
@@ -71,33 +103,93 @@ def _get(key: int) -> Binding:
     return b
 
 
+def _pad_rows_cols(t: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """t [r, c] zero-padded to [rows, cols] (byte view for fp8 / int8)."""
+    if tuple(t.shape) == (rows, cols):
+        return t.contiguous()
+    raw = t.view(torch.uint8) if t.element_size() == 1 else t
+    out = torch.zeros((rows, cols), dtype=raw.dtype, device=t.device)
+    out[:t.shape[0], :t.shape[1]] = raw
+    return out.view(t.dtype) if t.element_size() == 1 else out
+
+
+def _ref_weight(fmt: int, group: int, gpu: List[torch.Tensor], input_scale: Optional[torch.Tensor]) -> RefWeight:
+    """Reference-contract projection weights (native_runtime.cpp:286-311)."""
+    w = gpu[0]
+    bias = gpu[2] if len(gpu) > 2 and gpu[2] is not None and gpu[2].numel() else None
+    if fmt == 0:
+        b = None if bias is None else bias.to(torch.bfloat16).contiguous()
+        return RefWeight(0, group, w.to(torch.bfloat16).contiguous(), None, b, None, int(w.shape[0]),
+                         int(w.shape[1]))
+    ws = gpu[1].to(torch.float32).contiguous().reshape(-1)
+    n = int(w.shape[0])
+    if fmt == 1:
+        if group not in ref_ops.GROUPS4:
+            raise ValueError(f"INT4 projections use ConvRot groups {ref_ops.GROUPS4} or group 128 (got {group})")
+        if w.dtype not in (torch.int8, torch.uint8) or ws.numel() != n:
+            raise ValueError("INT4 projection: packed int8 [N, K/2] + fp32 per-channel scales [N] expected")
+        k = int(w.shape[1]) * 2
+        wd = w.view(torch.int8)
+    elif fmt == 2:
+        if w.dtype != torch.int8 or ws.numel() not in (1, n) or group not in (0,) + ref_ops.GROUPS4:
+            raise ValueError("INT8 projection: int8 [N, K] + fp32 scales [N] or [1], group 0/16/64/256")
+        k = int(w.shape[1])
+        wd = w
+    elif fmt in ref_ops.FP8_FORMATS:
+        if w.dtype != ref_ops.FP8_FORMATS[fmt][0] or ws.numel() not in (1, n):
+            raise ValueError(f"FP8 projection (format {fmt}): {ref_ops.FP8_FORMATS[fmt][0]} [N, K] + fp32 scale")
+        k = int(w.shape[1])
+        wd = w
+    else:
+        raise NotImplementedError(f"projection format {fmt}")
+    np_, kp = -(-n // 128) * 128, -(-k // 128) * 128
+    wd = _pad_rows_cols(wd, np_, kp // 2 if fmt == 1 else kp)
+    if ws.numel() == n and np_ != n:
+        ws = torch.cat([ws, ws.new_zeros(np_ - n)])
+    b = None
+    if bias is not None:
+        # gemm4 receives bias.to(fp32); the INT8 / FP8 routes bias.to(x dtype)
+        b = bias.to(torch.float32) if fmt == 1 else bias.to(torch.bfloat16).to(torch.float32)
+        b = torch.cat([b.reshape(-1), b.new_zeros(np_ - n)]).contiguous()
+    isc = None
+    if input_scale is not None and input_scale.numel():
+        isc = input_scale.to(torch.float32).reshape(1).contiguous()
+    return RefWeight(fmt, group, wd, ws, b, isc, n, k)
+
+
 def add_binding(key: int, kind: int, format: int, cpu: Sequence[torch.Tensor], gpu: Sequence[torch.Tensor],
                 vbar: Sequence[int], group: int, fuse: bool, eps: float, axes: Sequence[int], theta: float,
                 input_scale: torch.Tensor, optimize_io: bool) -> None:
     """Register module ``key`` (same arguments as native_runtime.cpp:528).
 
-    kind 0: ``gpu`` = [packed INT4 int8/uint8 [N, K/2], fp16 group scales
-    [N, K/128]] (format 1, group 128); converted once with prepare_weight.
-    kind 1: ``gpu[0]`` = fp32 RMSNorm weight ("w+1" form).  kind 2: ``axes``
-    and ``theta`` of the RoPE table.  kind 3/4: ``gpu[0]`` added to inputs.
-    ``cpu``, ``vbar`` and ``input_scale`` describe host copies and
+    kind 0: ``gpu`` = [weight, weight scale, optional bias], in the
+    checkpoint's format (format 0 plain; 1 INT4 packed [N, K/2] + fp32 [N]
+    with ConvRot group 16/64/256; 2 INT8 [N, K] + fp32 [N] or [1]; 3/4 FP8
+    [N, K] + fp32 scale, ``input_scale`` the static activation scale if
+    non-empty).  Format 1 with group 128 and fp16 group scales [N, K/128]
+    selects the group-128 W4A4 contract instead (converted once with
+    prepare_weight; no bias).  kind 1: ``gpu[0]`` = fp32 RMSNorm weight ("w+1"
+    form).  kind 2: ``axes`` and ``theta`` of the RoPE table.  kind 3/4:
+    ``gpu[0]`` added to inputs.  ``cpu`` and ``vbar`` describe host copies and
     virtual-memory staging of the reference's weight streaming; weights stay
     resident here, so they are accepted and not used."""
-    del cpu, vbar, input_scale
+    del cpu, vbar
     b = Binding(int(key), int(kind), int(format), int(group), bool(fuse), float(eps), [int(a) for a in axes],
                 float(theta), bool(optimize_io))
     gpu = list(gpu)
     if b.kind == 0:
-        if b.format != 1:
-            raise NotImplementedError("only INT4 (format 1) projections are served by the B200 build")
-        if b.group != ops.GROUP:
-            raise ValueError(f"INT4 projections use group-{ops.GROUP} scales (got {b.group})")
-        if len(gpu) > 2 and gpu[2] is not None:
-            raise NotImplementedError("projection bias is not part of the W4A4 block path")
-        packed, scales = gpu[0], gpu[1]
-        if packed.dtype == torch.int8:
-            packed = packed.view(torch.uint8)
-        b.weight = ops.prepare_weight(packed.contiguous(), scales.to(torch.float16).contiguous())
+        scales = gpu[1] if len(gpu) > 1 else None
+        group128 = (b.format == 1 and b.group == ops.GROUP and scales is not None and scales.dim() == 2 and
+                    scales.dtype == torch.float16)
+        if group128:
+            if len(gpu) > 2 and gpu[2] is not None and gpu[2].numel():
+                raise NotImplementedError("projection bias is not part of the group-128 W4A4 contract")
+            packed = gpu[0]
+            if packed.dtype == torch.int8:
+                packed = packed.view(torch.uint8)
+            b.weight = ops.prepare_weight(packed.contiguous(), scales.contiguous())
+        else:
+            b.ref = _ref_weight(b.format, b.group, gpu, input_scale)
     elif b.kind == 1:
         b.tensors = [gpu[0].to(torch.float32).contiguous()]
     elif b.kind in (3, 4):
@@ -176,9 +268,13 @@ def _norm(key: int) -> Binding:
 
 def _proj(key: int) -> Binding:
     b = _get(key)
-    if b.kind != 0 or b.weight is None:
-        raise RuntimeError(f"binding {key} is not an INT4 projection")
+    if b.kind != 0 or (b.weight is None and b.ref is None):
+        raise RuntimeError(f"binding {key} is not a projection")
     return b
+
+
+def _width(b: Binding) -> int:
+    return b.weight.n if b.weight is not None else b.ref.n
 
 
 def _rows_len(x: torch.Tensor):
@@ -189,12 +285,183 @@ def _rows_len(x: torch.Tensor):
 
 
 def _packed(qa: torch.Tensor, qs: torch.Tensor, K: int):
+    """Group-128 packed activation: uint8 codes + fp16 [rows, K/128]."""
     if qa.dtype == torch.int8:
         qa = qa.view(torch.uint8)
     if qa.dtype != torch.uint8 or qs.dtype != torch.float16:
         raise RuntimeError("Invalid packed normalized activation (int8 codes + fp16 group scales expected)")
     rows = qa.numel() * 2 // K
     return qa.reshape(rows, K // 2), qs.reshape(rows, K // ops.GROUP)
+
+
+def _ref_prepared(x: torch.Tensor, qa: torch.Tensor, qs: torch.Tensor, keys: Sequence[int]):
+    """The reference's prepared_input checks (native_runtime.cpp:447-453):
+    int8 codes [rows, K/2], one fp32 scale per row, every key INT4 of one
+    ConvRot group."""
+    if not (qa.dtype == torch.int8 and qs.dtype == torch.float32 and qa.is_contiguous() and qs.is_contiguous() and
+            qa.device == x.device and qs.device == x.device and qa.numel() * 2 == x.numel() and
+            qs.numel() == x.numel() // x.shape[-1]):
+        raise RuntimeError("Invalid packed normalized activation")
+    group = _get(keys[0]).group
+    for k in keys:
+        b = _get(k)
+        if b.ref is None or b.format != 1 or b.group != group:
+            raise RuntimeError("Packed input cannot be shared across incompatible quantization layouts")
+    rows = qs.numel()
+    return qa.reshape(rows, -1), qs.reshape(rows, 1)
+
+
+def _freqs_for(freqs: torch.Tensor, length: int) -> torch.Tensor:
+    f = freqs.to(torch.float32).contiguous()
+    if f.numel() != length * 64 * 4:
+        raise RuntimeError("RoPE table must be batch-shared fp32 [.., L, 64, 2, 2]")
+    return f.reshape(length, 64, 2, 2)
+
+
+# ----------------------------------------- reference contract (Binding.ref)
+
+
+def _ref_quantize(x2: torch.Tensor, r: RefWeight):
+    """native_runtime.cpp:266-285: per-row INT4 / INT8 after ConvRot, or FP8
+    with one scale (the binding's input scale, else amax / fmax)."""
+    if r.format == 1:
+        return ref_ops.quant4(x2, r.group)
+    if r.format == 2:
+        return ref_ops.quant8(x2, r.group)
+    scale = r.input_scale if r.input_scale is not None else ref_ops.fp8_scale(x2, r.format)
+    return ref_ops.fp8_quant(x2, r.format, scale), scale
+
+
+def _pad_k(q: torch.Tensor, r: RefWeight) -> torch.Tensor:
+    kq = r.w.shape[1]
+    if q.shape[1] == kq:
+        return q
+    return _pad_rows_cols(q, q.shape[0], kq)
+
+
+def _ref_project(x2: torch.Tensor, r: RefWeight, q=None) -> torch.Tensor:
+    """T(acc * xs * ws [+ bias]) of rows x2 bf16 [m, K] (native_runtime.cpp:
+    286-311), bf16 [m, n]."""
+    if r.format == 0:
+        return torch.nn.functional.linear(x2, r.w, r.bias)
+    qa, qs = _ref_quantize(x2, r) if q is None else q
+    qa = _pad_k(qa, r)
+    if r.format == 1:
+        out = ref_ops.gemm4(qa, qs.reshape(-1), r.w, r.ws, r.bias)
+    elif r.format == 2:
+        out = ref_ops.gemm8(qa, qs.reshape(-1), r.w, r.ws, r.bias)
+    else:
+        out = ref_ops.gemm_f8(qa, qs.reshape(-1), r.w, r.ws, r.bias)
+    return out[:, :r.n] if out.shape[1] != r.n else out
+
+
+def _ref_cache_key(b: Binding, i: int):
+    """Bindings that quantise the input alike share one quantisation
+    (native_runtime.cpp:336-340)."""
+    if not b.fuse:
+        return ("own", i)
+    isc = b.ref.input_scale
+    return (b.format, b.group, None if isc is None else isc.data_ptr())
+
+
+def _linear(x: torch.Tensor, key: int, gate: Optional[torch.Tensor] = None,
+            residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """native_runtime.cpp:325-332: one projection, optionally
+    out = T(residual + T(T(p) * gate)) (fused into the GEMM for INT4)."""
+    b = _proj(key)
+    if b.weight is not None:
+        return _linear_gated(x, key, gate, residual)
+    r = b.ref
+    rows, length, K = _rows_len(x)
+    x2 = x.reshape(rows, K).contiguous()
+    shape = list(x.shape[:-1]) + [r.n]
+    if gate is not None and r.format == 1 and b.fuse and r.bias is None and not r.padded:
+        g = gate.reshape(-1, r.n).contiguous()
+        if g.shape[0] == 1 and rows // length > 1:
+            g = g.expand(rows // length, r.n).contiguous()
+        qa, qs = ref_ops.quant4(x2, r.group)
+        b.count("gated_gemm")
+        out = ref_ops.gated_residual(qa, qs.reshape(-1), r.w, r.ws, g, residual.reshape(rows, r.n).contiguous(),
+                                     length=length)
+        return out.reshape(residual.shape)
+    out = _ref_project(x2, r).reshape(shape)
+    b.count("gemm")
+    if gate is None:
+        return out
+    if gate.dim() > 0 and gate.numel() != gate.shape[-1]:
+        return residual + gate * out
+    return ops.elementwise(gate.contiguous(), out.contiguous(), residual.contiguous(), 2, int(gate.numel()))
+
+
+def _all_int4(bs: Sequence[Binding]) -> bool:
+    g = bs[0].group
+    return all(b.ref is not None and b.format == 1 and b.group == g and b.ref.bias is None and not b.ref.padded
+               for b in bs)
+
+
+def _group(x: torch.Tensor, keys: Sequence[int], prepared=None) -> List[torch.Tensor]:
+    """Plain projections of x by each key (native_runtime.cpp:333-358), bf16
+    [rows, n]; one quantisation per input layout."""
+    rows, _, K = _rows_len(x)
+    x2 = x.reshape(rows, K).contiguous()
+    cache = {}
+    outs = []
+    for i, key in enumerate(keys):
+        b = _proj(key)
+        if b.weight is not None:
+            if ("b128",) not in cache:
+                cache[("b128",)] = ops.rotate_quant(x2) if prepared is None else prepared
+            a, sa = cache[("b128",)]
+            outs.append(ops.gemm_bf16(a, sa, b.weight))
+            continue
+        ck = _ref_cache_key(b, i)
+        if b.format != 0 and ck not in cache:
+            cache[ck] = _ref_quantize(x2, b.ref) if prepared is None else prepared
+        outs.append(_ref_project(x2, b.ref, cache.get(ck)))
+    return outs
+
+
+def _head_norm(p: torch.Tensor, B: int, L: int, nb: Binding) -> torch.Tensor:
+    """Per-head RMSNorm of a projection [B*L, H*128] -> [B, H, L, 128]
+    (native_runtime.cpp:352-354)."""
+    h = p.shape[-1] // HEAD_DIM
+    y = ops.norm_mod(p.reshape(B * L * h, HEAD_DIM).contiguous(), nb.tensors[0], eps=nb.eps)
+    return y.view(B, L, h, HEAD_DIM).transpose(1, 2)
+
+
+def _split_qkv(x, keys, norms, freqs, heads, kvheads, prepared=None, sigmoid_gate=True):
+    """The reference's split route: group projections, per-head norm, RoPE
+    (native_runtime.cpp:333-358, 460-478)."""
+    B, L = int(x.shape[0]), int(x.shape[1])
+    p = _group(x, keys, prepared)
+    nq, nk = _norm(norms[0]), _norm(norms[1])
+    q = _head_norm(p[0], B, L, nq)
+    k = _head_norm(p[1], B, L, nk)
+    if freqs is not None:
+        fb = freqs.to(torch.float32).contiguous()
+        q, k = ops.rope(q.contiguous(), k.contiguous(), fb)
+    g = p[3] if len(p) > 3 else None
+    if g is not None and sigmoid_gate:
+        g = ops.elementwise(g.contiguous(), None, None, 1)
+    v = p[2].view(B, L, -1)
+    return q, k, v, None if g is None else g.view(B, L, -1)
+
+
+def _ref_qkv(x, qa, qs, freqs, keys, norms, heads, kvheads, sigmoid_gate=True):
+    """Joint INT4 QKV over the reference contract (kernels/joint_projection.cu:
+    222-225 semantics): Q/K RMSNorm + RoPE in the epilogue, V plain, the gate
+    sigmoided."""
+    B, L = int(x.shape[0]), int(x.shape[1])
+    bs = [_proj(k) for k in keys]
+    nq, nk = _norm(norms[0]), _norm(norms[1])
+    q, k, v, g = ref_ops.qkv(qa, qs.reshape(-1), [b.ref.w for b in bs], [b.ref.ws for b in bs], nq.tensors[0],
+                             nk.tensors[0], _freqs_for(freqs, L), length=L, eps_q=nq.eps, eps_k=nk.eps,
+                             sigmoid_gate=sigmoid_gate)
+    return (q.view(B, L, heads, HEAD_DIM).transpose(1, 2), k.view(B, L, kvheads, HEAD_DIM).transpose(1, 2),
+            v.view(B, L, kvheads * HEAD_DIM), None if g is None else g.view(B, L, heads * HEAD_DIM))
+
+
+# ----------------------------------------- group-128 contract (Binding.weight)
 
 
 def _linear_gated(x: torch.Tensor, key: int, gate: Optional[torch.Tensor], residual: Optional[torch.Tensor]):
@@ -214,11 +481,21 @@ def _linear_gated(x: torch.Tensor, key: int, gate: Optional[torch.Tensor], resid
     return out.reshape(residual.shape)
 
 
-def _freqs_for(freqs: torch.Tensor, length: int) -> torch.Tensor:
-    f = freqs.to(torch.float32).contiguous()
-    if f.numel() != length * 64 * 4:
-        raise RuntimeError("RoPE table must be batch-shared fp32 [.., L, 64, 2, 2]")
-    return f.reshape(length, 64, 2, 2)
+def _b128_qkv(x, a, s, freqs, keys, heads, kvheads, norms, sigmoid_gate=True):
+    B, L = int(x.shape[0]), int(x.shape[1])
+    wq, wk, wv, wg = (_proj(k) for k in keys)
+    nq, nk = _norm(norms[0]), _norm(norms[1])
+    if wq.weight.n != heads * HEAD_DIM or wk.weight.n != kvheads * HEAD_DIM or wv.weight.n != kvheads * HEAD_DIM:
+        raise RuntimeError("qkv weight widths do not match heads / kvheads")
+    q, k, v, g = ops.qkv(a, s, wq.weight, wk.weight, wv.weight, nq.tensors[0], nk.tensors[0],
+                         _freqs_for(freqs, L), length=L, eps_q=nq.eps, eps_k=nk.eps,
+                         wg=wg.weight if sigmoid_gate else None)
+    if not sigmoid_gate:
+        g = ops.gemm_bf16(a, s, wg.weight)
+    # token-major storage viewed as [B, H, L, D] (native_runtime.cpp:413-422)
+    q = q.view(B, L, heads, HEAD_DIM).transpose(1, 2)
+    k = k.view(B, L, kvheads, HEAD_DIM).transpose(1, 2)
+    return q, k, v.view(B, L, kvheads * HEAD_DIM), g.view(B, L, heads * HEAD_DIM)
 
 
 # ------------------------------------------------------------- op bodies
@@ -227,10 +504,16 @@ def _freqs_for(freqs: torch.Tensor, length: int) -> torch.Tensor:
 def _norm_quant(x, scale, shift, norm_key, target_key, cut):
     nb, tb = _norm(norm_key), _get(target_key)
     rows, length, K = _rows_len(x)
-    if tb.format != 1 or tb.group != ops.GROUP or nb.tensors[0].numel() != K:
+    if tb.kind != 0 or tb.format != 1 or nb.tensors[0].numel() != K:
         raise RuntimeError("Normalized quantization requires compatible INT4 input")
-    q, s = ops.norm_quant(x.reshape(rows, K).contiguous(), nb.tensors[0], scale.reshape(-1, K).contiguous(),
-                          shift.reshape(-1, K).contiguous(), length=length, cut=int(cut), eps=nb.eps)
+    x2 = x.reshape(rows, K).contiguous()
+    sc, sh = scale.reshape(-1, K).contiguous(), shift.reshape(-1, K).contiguous()
+    if tb.ref is not None:
+        q, s = ref_ops.norm_quant4(x2, nb.tensors[0], sc, sh, length=length, cut=int(cut), eps=nb.eps,
+                                   group=tb.group)
+        nb.count("norm_quant_fused")
+        return q, s
+    q, s = ops.norm_quant(x2, nb.tensors[0], sc, sh, length=length, cut=int(cut), eps=nb.eps)
     nb.count("norm_quant_fused")
     return q.view(torch.int8), s
 
@@ -244,80 +527,110 @@ def _norm_mod(x, scale, shift, key, cut):
 
 
 def _gated(x, gate, residual, key):
-    return _linear_gated(x, key, gate, residual)
+    return _linear(x, key, gate, residual)
 
 
 def _gated_norm_quant(x, gate, residual, scale, shift, key, norm_key, target_key, cut):
-    out = _linear_gated(x, key, gate, residual)
+    out = _linear(x, key, gate, residual)
     q, s = _norm_quant(out, scale, shift, norm_key, target_key, cut)
     return out, q, s
 
 
 def _residual_norm(x, gate, residual, scale, shift, key, norm_key):
-    out = _linear_gated(x, key, gate, residual)
+    out = _linear(x, key, gate, residual)
     return out, _norm_mod(out, scale, shift, norm_key, -1)
 
 
-def _qkv_common(x, qa, qs, freqs, keys, norms, heads, kvheads):
-    B, L = int(x.shape[0]), int(x.shape[1])
-    K = int(x.shape[-1])
-    a, s = _packed(qa, qs, K)
-    wq, wk, wv, wg = (_proj(k) for k in keys)
-    nq, nk = _norm(norms[0]), _norm(norms[1])
-    if wq.weight.n != heads * HEAD_DIM or wk.weight.n != kvheads * HEAD_DIM or wv.weight.n != kvheads * HEAD_DIM:
-        raise RuntimeError("qkv weight widths do not match heads / kvheads")
-    q, k, v, g = ops.qkv(a, s, wq.weight, wk.weight, wv.weight, nq.tensors[0], nk.tensors[0],
-                         _freqs_for(freqs, L), length=L, eps_q=nq.eps, eps_k=nk.eps, wg=wg.weight)
-    wq.count("prepared_qkv")
-    # token-major storage viewed as [B, H, L, D] (native_runtime.cpp:413-422)
-    q = q.view(B, L, heads, HEAD_DIM).transpose(1, 2)
-    k = k.view(B, L, kvheads, HEAD_DIM).transpose(1, 2)
-    return q, k, v.view(B, L, kvheads * HEAD_DIM), g.view(B, L, heads * HEAD_DIM)
-
-
 def _qkv_prepared(x, qa, qs, freqs, keys, norms, heads, kvheads):
-    return _qkv_common(x, qa, qs, freqs, keys, norms, heads, kvheads)
+    bs = [_proj(k) for k in keys]
+    bs[0].count("prepared_qkv")
+    if qs.dtype == torch.float32:
+        a, s = _ref_prepared(x, qa, qs, keys)
+        if _all_int4(bs):
+            return _ref_qkv(x, a, s, freqs, keys, norms, heads, kvheads)
+        return _split_qkv(x, keys, norms, freqs, heads, kvheads, prepared=(a, s))
+    a, s = _packed(qa, qs, int(x.shape[-1]))
+    return _b128_qkv(x, a, s, freqs, keys, heads, kvheads, norms)
 
 
 def _joint_qkv(x, freqs, keys, norms, heads, kvheads):
+    bs = [_proj(k) for k in keys]
     rows, _, K = _rows_len(x)
-    qa, qs = ops.rotate_quant(x.reshape(rows, K).contiguous())
-    return _qkv_common(x, qa, qs, freqs, keys, norms, heads, kvheads)
+    if all(b.weight is not None for b in bs):
+        a, s = ops.rotate_quant(x.reshape(rows, K).contiguous())
+        bs[0].count("joint_qkv")
+        return _b128_qkv(x, a, s, freqs, keys, heads, kvheads, norms)
+    if _all_int4(bs):
+        a, s = ref_ops.quant4(x.reshape(rows, K).contiguous(), bs[0].group)
+        bs[0].count("joint_qkv")
+        return _ref_qkv(x, a, s, freqs, keys, norms, heads, kvheads)
+    bs[0].count("routed_qkv_split")
+    return _split_qkv(x, keys, norms, freqs, heads, kvheads)
 
 
-def _swiglu_common(x, qa, qs, keys, width):
-    K = int(x.shape[-1])
-    a, s = _packed(qa, qs, K)
+def _swiglu_common(x, a, s, keys, width):
     wg, wu = _proj(keys[0]), _proj(keys[1])
-    if wg.weight.n != width or wu.weight.n != width:
+    if _width(wg) != width or _width(wu) != width:
         raise RuntimeError("Joint SwiGLU weight contract changed")
-    wg.count("prepared_swiglu")
-    return ops.swiglu_bf16(a, s, wg.weight, wu.weight).reshape(list(x.shape[:-1]) + [width])
+    shape = list(x.shape[:-1]) + [width]
+    if wg.weight is not None and wu.weight is not None:
+        return ops.swiglu_bf16(a, s, wg.weight, wu.weight).reshape(shape)
+    if _all_int4([wg, wu]):
+        return ref_ops.swiglu(a, s.reshape(-1), wg.ref.w, wg.ref.ws, wu.ref.w, wu.ref.ws).reshape(shape)
+    raise RuntimeError("Joint SwiGLU weight contract changed")
 
 
 def _swiglu_prepared(x, qa, qs, keys, width):
-    return _swiglu_common(x, qa, qs, keys, width)
+    _proj(keys[0]).count("prepared_swiglu")
+    if qs.dtype == torch.float32:
+        a, s = _ref_prepared(x, qa, qs, keys)
+    else:
+        a, s = _packed(qa, qs, int(x.shape[-1]))
+    return _swiglu_common(x, a, s, keys, width)
 
 
 def _joint_swiglu(x, keys, width):
     rows, _, K = _rows_len(x)
-    qa, qs = ops.rotate_quant(x.reshape(rows, K).contiguous())
-    return _swiglu_common(x, qa, qs, keys, width)
+    bs = [_proj(k) for k in keys]
+    x2 = x.reshape(rows, K).contiguous()
+    if all(b.weight is not None for b in bs):
+        a, s = ops.rotate_quant(x2)
+    elif _all_int4(bs):
+        a, s = ref_ops.quant4(x2, bs[0].group)
+    else:
+        bs[0].count("routed_swiglu_split")
+        pg, pu = _group(x, keys)
+        return ops.elementwise(pg.contiguous(), pu.contiguous(), None, 0).reshape(list(x.shape[:-1]) + [width])
+    bs[0].count("joint_swiglu")
+    return _swiglu_common(x, a, s, keys, width)
 
 
 def _project_many(x, keys, widths):
-    outs = [_linear_gated(x, k, None, None) for k in keys]
+    outs = _group(x, keys)
     for o, w in zip(outs, widths):
         if o.shape[-1] != w:
             raise RuntimeError("projection width mismatch")
-    return outs
+    return [o.reshape(list(x.shape[:-1]) + [o.shape[-1]]) for o in outs]
 
 
 def _attention_inputs(x, freqs, keys, widths, norms, heads, kvheads):
-    if freqs is None or len(norms) != 2:
+    """native_runtime.cpp:601 (group with norms): Q and K per-head normalised
+    (and RoPE'd when freqs is given) as [B, H, L, 128], V and the gate as
+    plain projections [B, L, n] -- the gate is NOT sigmoided here (the graph
+    passes gate_is_sigmoid=False for this route, graph_model.py:39-44)."""
+    if len(norms) != 2:
         outs = _project_many(x, keys, widths)
         return outs[0], outs[1], outs[2], outs[3]
-    return _joint_qkv(x, freqs, keys, norms, heads, kvheads)
+    bs = [_proj(k) for k in keys]
+    if freqs is not None and all(b.weight is not None for b in bs):
+        rows, _, K = _rows_len(x)
+        a, s = ops.rotate_quant(x.reshape(rows, K).contiguous())
+        return _b128_qkv(x, a, s, freqs, keys, heads, kvheads, norms, sigmoid_gate=False)
+    if freqs is not None and _all_int4(bs):
+        rows, _, K = _rows_len(x)
+        a, s = ref_ops.quant4(x.reshape(rows, K).contiguous(), bs[0].group)
+        return _ref_qkv(x, a, s, freqs, keys, norms, heads, kvheads, sigmoid_gate=False)
+    return _split_qkv(x, keys, norms, freqs, heads, kvheads, sigmoid_gate=False)
 
 
 def _sdpa(q, k, v, enable_gqa):
@@ -327,7 +640,7 @@ def _sdpa(q, k, v, enable_gqa):
 def _managed(x, key, kind, width):
     b = _get(key)
     if kind == 0:
-        return _linear_gated(x, key, None, None)
+        return _linear(x, key)
     if kind == 1:
         rows, _, K = _rows_len(x)
         return ops.norm_mod(x.reshape(rows, K).contiguous(), b.tensors[0], eps=b.eps).reshape(x.shape)
@@ -419,8 +732,11 @@ def _e(shape, like, dtype=None):
     return torch.empty(shape, device=like.device, dtype=like.dtype if dtype is None else dtype)
 
 
-def _fake_packed(x):
+def _fake_packed(x, target_key):
     rows, K = math.prod(x.shape[:-1]), x.shape[-1]
+    b = _records.get(int(target_key))
+    if b is not None and b.ref is not None:
+        return _e((rows, K // 2), x, torch.int8), _e((rows, 1), x, torch.float32)
     return _e((rows, K // 2), x, torch.int8), _e((rows, K // ops.GROUP), x, torch.float16)
 
 
@@ -433,15 +749,15 @@ def _fake_qkv(x, heads, kvheads):
 
 def _fake_width(x, key):
     b = _records.get(int(key))
-    if b is None or b.weight is None:
+    if b is None or (b.weight is None and b.ref is None):
         raise RuntimeError(f"Native K2 binding released: {key}")
-    return b.weight.n
+    return _width(b)
 
 
 FAKES = {
-    "norm_quant": lambda x, scale, shift, norm_key, target_key, cut: _fake_packed(x),
+    "norm_quant": lambda x, scale, shift, norm_key, target_key, cut: _fake_packed(x, target_key),
     "gated_norm_quant": lambda x, gate, residual, scale, shift, key, norm_key, target_key, cut:
-        (torch.empty_like(residual, memory_format=torch.contiguous_format), *_fake_packed(residual)),
+        (torch.empty_like(residual, memory_format=torch.contiguous_format), *_fake_packed(residual, target_key)),
     "qkv_prepared": lambda x, qa, qs, freqs, keys, norms, heads, kvheads: _fake_qkv(x, heads, kvheads),
     "swiglu_prepared": lambda x, qa, qs, keys, width: _e(tuple(x.shape[:-1]) + (width,), x),
     "sdpa": lambda q, k, v, enable_gqa: _e((q.shape[0], q.shape[2], q.shape[1] * q.shape[3]), q),
@@ -486,5 +802,5 @@ def _kohaku_fa_fake(q, k, v, mask, gate, gate_is_sigmoid):
     return torch.empty((q.shape[0], q.shape[2], q.shape[1] * q.shape[3]), device=q.device, dtype=q.dtype)
 
 
-__all__ = ["Binding", "add_binding", "release_bindings", "configure", "configure_joint", "configure_norm_quant",
+__all__ = ["Binding", "RefWeight", "add_binding", "release_bindings", "configure", "configure_joint", "configure_norm_quant",
            "set_route", "finish_tuning", "set_lookahead", "reset_stats", "stats", "kohaku_fa", "SCHEMAS"]

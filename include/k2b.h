@@ -230,6 +230,28 @@ int k2b_gated_residual_e4m3(const void* a8, const void* sa, const void* w, const
 int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
                           const void* su, void* h8, void* hs, int m, int width, int k, void* stream);
 
+/* ------------------------------------ INT8 / FP8 weights, reference contract --
+ * Projections of INT8 / FP8 checkpoint weights (the reference's formats 2 and
+ * 3/4: at::_int_mm + k2_dequant8, at::_scaled_mm; native_runtime.cpp:271-283,
+ * 298-311) on the tcgen05 pair GEMM, the whole of k in one accumulator and the
+ * dequant fused: out bf16 = bf16(fp32(fp32(acc*xs[r*xs_stride])*ws[c*ws_stride])
+ * + bias[c]); strides 0 = one scale; bias fp32 [n] or null; k, n % 128 == 0.
+ * k2b_gemm8: int8 a8 [m,k] / w8 [n,k].  k2b_gemm_f8: fp8 with afmt / bfmt
+ * 0 = e4m3, 1 = e5m2.
+ * k2b_ref_qkv / k2b_ref_gated_residual: k2_int4_qkv / k2_int4_gated_residual
+ * (reference contract) over `batch` latents of `length` tokens (RoPE token =
+ * row % length, gate row = row / length, gate bf16 [batch, n]). */
+int k2b_gemm8(const void* a8, const void* xs, int xs_stride, const void* w8, const void* ws, int ws_stride,
+              const void* bias, void* out, int m, int n, int k, void* stream);
+int k2b_gemm_f8(const void* a8, const void* xs, int xs_stride, const void* w8, const void* ws, int ws_stride,
+                const void* bias, void* out, int m, int n, int k, int afmt, int bfmt, void* stream);
+int k2b_ref_qkv(const void* a, const void* xs, const void* wq, const void* sq, const void* wk, const void* sk,
+                const void* wv, const void* sv, const void* wg, const void* sg, const void* nq, const void* nk,
+                const void* freq, void* qo, void* ko, void* vo, void* go, int m, int length, int qwidth, int kvwidth,
+                int k, float eq, float ek, void* stream);
+int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const void* ws, const void* gate,
+                           const void* residual, void* out, int m, int length, int n, int k, void* stream);
+
 /* ------------------------------------------------------------ block loop --
  * Native loop over transformer blocks (replaces the compiled entry that
  * NativeGraph::run drives, native_runtime.cpp:543-571, over graph_model.py's

@@ -90,6 +90,30 @@ def test_qkv_prepared_layout_and_parity(cuda, reg):
     assert torch.equal(v.reshape(B * L, -1), ref[2]) and torch.equal(g.reshape(B * L, -1), ref[3])
 
 
+def test_attention_inputs_returns_the_raw_gate(cuda, reg):
+    """attention_inputs (native_runtime.cpp:601) normalises Q/K and RoPEs them
+    but leaves the gate as the plain projection: the graph passes
+    gate_is_sigmoid=False for this route (graph_model.py:42-44)."""
+    import torch
+    from k2b import native_ops as N
+    from k2b import ops
+    from k2b.model import rope_positions, rope_table
+
+    x = t_bf16(bf16_x(B * L, K, 16, outliers=False), cuda).view(B, L, K)
+    freqs = rope_table(rope_positions(4, 4, 9), (64, 64), 10000.0).to(cuda).view(1, 1, L, 64, 2, 2)
+    keys = [reg[n][0] for n in ("wq", "wk", "wv", "wg")]
+    norms = [reg["qnorm"][0], reg["knorm"][0]]
+    q, k, v, g = torch.ops.k2_native.attention_inputs(x, freqs, keys, [H * 128, HK * 128, HK * 128, H * 128], norms,
+                                                      H, HK)
+    jq, jk, jv, jg = torch.ops.k2_native.joint_qkv(x, freqs, keys, norms, H, HK)
+    assert torch.equal(q, jq) and torch.equal(k, jk) and torch.equal(v, jv)
+    a, sa = ops.rotate_quant(x.reshape(B * L, K))
+    raw = ops.gemm_bf16(a, sa, N._get(keys[3]).weight)
+    assert torch.equal(g.reshape(B * L, -1), raw)
+    # joint_qkv's gate is sigmoid(p) of the same projection
+    assert float((jg.reshape(B * L, -1).float() - torch.sigmoid(raw.float())).abs().max()) <= 8e-3
+
+
 def test_swiglu_prepared_bitexact(cuda, reg):
     import torch
 

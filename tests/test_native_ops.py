@@ -87,8 +87,48 @@ def test_registry_lifecycle():
         N._get(9001)
     with pytest.raises(ValueError):
         N.add_binding(9003, 0, 1, [], [w, w], [], 64, True, 1e-6, [], 1000.0, torch.empty(0), True)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError):  # INT8 projection with float weights
         N.add_binding(9004, 0, 2, [], [w, w], [], 128, True, 1e-6, [], 1000.0, torch.empty(0), True)
+    with pytest.raises(NotImplementedError):
+        N.add_binding(9005, 0, 7, [], [w, w], [], 128, True, 1e-6, [], 1000.0, torch.empty(0), True)
+
+
+def test_reference_contract_bindings_keep_the_checkpoint_format():
+    """Format 1 (ConvRot group 64, per-channel fp32 scales), 2 (INT8) and 3
+    (FP8 e4m3) bindings keep the checkpoint's own layout, zero-padded to the
+    GEMM's 128 (registration touches no kernel)."""
+    g = torch.Generator().manual_seed(3)
+    n, k = 200, 1000
+    packed = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8)
+    ws = torch.rand(n, generator=g)
+    bias = torch.randn(n, generator=g)
+    N.add_binding(9101, 0, 1, [], [packed, ws, bias], [], 64, True, 1e-6, [], 1000.0, torch.empty(0), True)
+    r = N._get(9101).ref
+    assert N._get(9101).weight is None and r.format == 1 and r.group == 64 and (r.n, r.k) == (n, k)
+    assert r.w.shape == (256, 512) and r.w.dtype == torch.int8 and r.padded
+    assert torch.equal(r.w[:n, :k // 2], packed) and not r.w[n:].any() and not r.w[:, k // 2:].any()
+    assert torch.equal(r.ws[:n], ws) and not r.ws[n:].any()
+    assert torch.equal(r.bias[:n], bias)  # fp32 as k2_gemm4 receives it
+    w8 = torch.randint(-127, 128, (256, 1024), generator=g, dtype=torch.int8)
+    N.add_binding(9102, 0, 2, [], [w8, torch.rand(1), bias[:128].repeat(2)], [], 0, True, 1e-6, [], 1000.0,
+                  torch.empty(0), True)
+    r = N._get(9102).ref
+    assert r.w.shape == (256, 1024) and not r.padded and r.ws.numel() == 1
+    assert torch.equal(r.bias, bias[:128].repeat(2).to(torch.bfloat16).float())  # rounded to the x dtype
+    w3 = torch.randn(128, 256, generator=g).to(torch.float8_e4m3fn)
+    N.add_binding(9103, 0, 3, [], [w3, torch.tensor(0.5)], [], 0, True, 1e-6, [], 1000.0, torch.tensor([0.25]),
+                  True)
+    r = N._get(9103).ref
+    assert r.w.dtype == torch.float8_e4m3fn and float(r.input_scale) == 0.25
+    with pytest.raises(ValueError):  # INT4 with a group the ConvRot quantiser does not have
+        N.add_binding(9104, 0, 1, [], [packed, ws], [], 32, True, 1e-6, [], 1000.0, torch.empty(0), True)
+    x = _m(1, 7, 1024)
+    N.add_binding(9105, 1, 0, [], [torch.rand(1024)], [], 0, False, 1e-6, [], 1000.0, torch.empty(0), True)
+    N.add_binding(9106, 0, 1, [], [torch.zeros(128, 512, dtype=torch.int8), torch.rand(128)], [], 256, True, 1e-6,
+                  [], 1000.0, torch.empty(0), True)
+    q, s = torch.ops.k2_native.norm_quant(x, _m(1, 1024), _m(1, 1024), 9105, 9106, -1)
+    assert q.shape == (7, 512) and q.dtype == torch.int8 and s.shape == (7, 1) and s.dtype == torch.float32
+    N.release_bindings([9101, 9102, 9103, 9105, 9106])
 
 
 def test_cpu_tensors_reach_no_kernel():
