@@ -7,14 +7,19 @@
 // (gate_kind 1: sigmoid applied here, 2: gate already sigmoided), and a fused
 // H128 rotation + group-128 INT4 quantisation of o for the out-projection.
 //
-// One CTA = one 128-token Q tile of two Q heads that share a KV head, so every
-// K/V tile brought in by TMA feeds both heads' MMAs.  TMEM (512 columns):
+// One CTA owns two Q slots that read the same KV head, so every K/V tile
+// brought in by TMA feeds both slots' MMAs:
+//   * even GQA group (the Krea2 blocks, 48/12): one 128-token Q tile of two Q
+//     heads 2p, 2p+1 (grid.y = heads / 2);
+//   * odd group (group 1: the text-fusion blocks, 20/20): two consecutive
+//     128-token Q tiles of one head (grid.y = heads, p.qpair = 1).
+// TMEM (512 columns):
 //   S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512)
 // P_t (bf16, 64 packed columns) overwrites S_t after the softmax has read it;
 // tcgen05.mma ops of the issuing thread execute in order, so the next S MMA
 // into the same columns follows the PV MMA that reads P.
 // Roles (384 threads): warp 0 TMA loads, warp 1 TMEM alloc + MMA issue,
-// warps 4-7 softmax/epilogue of head 2p, warps 8-11 of head 2p+1.
+// warps 4-7 softmax/epilogue of slot 0, warps 8-11 of slot 1.
 // O is rescaled in TMEM only when a row's running max grows by more than
 // 2^8 in exp2 units (the max used for P may lag the true max); the final
 // o = acc/l is unchanged by that choice up to rounding.
@@ -50,6 +55,7 @@ struct AttnParams {
   uint8_t* oq;                      // [B*lq, heads*D/2] packed, [B*lq, heads*D] e4m3 bytes, or null
   __half* os;                       // [B*lq, heads] fp16 scales
   int oq_bytes;                     // oq holds e4m3 bytes (the block loop's container)
+  int qpair;                        // slots = two Q tiles of one head (odd GQA group)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -75,11 +81,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * FA_BM;
-  const int pair = blockIdx.y;
   const int b = blockIdx.z;
   const int group = p.heads / p.kvheads;
-  const int h0 = 2 * pair;
+  // slot t: head h0 + t*hstep, tokens [q0 + t*qstep, +128)
+  const int h0 = p.qpair ? blockIdx.y : 2 * blockIdx.y;
+  const int hstep = p.qpair ? 0 : 1;
+  const int q0 = blockIdx.x * (p.qpair ? 2 * FA_BM : FA_BM);
+  const int qstep = p.qpair ? FA_BM : 0;
   const int hk = h0 / group;
   const int nkv = (p.lk + FA_BN - 1) / FA_BN;
 
@@ -116,8 +124,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_arrive_expect_tx(q_full, 2 * FA_TILE_BYTES);
       for (int t = 0; t < 2; ++t)
         for (int hb = 0; hb < 2; ++hb)
-          tma_load_4d(smem + FA_OFF_Q + t * FA_TILE_BYTES + hb * (FA_TILE_BYTES / 2), &maps.q, q_full, hb * 64, q0,
-                      h0 + t, b);
+          tma_load_4d(smem + FA_OFF_Q + t * FA_TILE_BYTES + hb * (FA_TILE_BYTES / 2), &maps.q, q_full, hb * 64,
+                      q0 + t * qstep, h0 + t * hstep, b);
       q_issued = true;
       for (int j = 0; j < nkv; ++j) {
         const int s = j % FA_KV_STAGES;
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ softmax + epilogue
-    const int t = (warp - 4) >> 2;  // which head of the pair
+    const int t = (warp - 4) >> 2;  // which slot
     const int q = warp & 3;
     const int r = 32 * q + lane;    // row within the Q tile
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
@@ -279,8 +287,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     // ------------------------------------------------------ epilogue
     if (ok && mbar_wait(&o_full[t], (nkv - 1) & 1, abort_flag, ERR_WAIT_SOFTMAX)) {
       tc_fence_after();
-      const int tok = q0 + r;
-      const int h = h0 + t;
+      const int tok = q0 + t * qstep + r;
+      const int h = h0 + t * hstep;
       const float inv_l = l_run > 0.0f ? __frcp_rn(l_run) : 0.0f;
       float o[128];
 #pragma unroll

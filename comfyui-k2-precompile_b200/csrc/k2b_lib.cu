@@ -307,8 +307,7 @@ static int attention_launch(const void* q, const void* k, const void* v, const v
                             long long q_sh, long long q_st, long long k_sb, long long k_sh, long long k_st,
                             long long v_sb, long long v_sh, long long v_st, int gate_kind, cudaStream_t st,
                             bool oq_bytes = false) {
-  if (batch <= 0 || heads <= 0 || kvheads <= 0 || heads % kvheads || (heads / kvheads) % 2 || lq <= 0 || lk <= 0 ||
-      dim != FA_D)
+  if (batch <= 0 || heads <= 0 || kvheads <= 0 || heads % kvheads || lq <= 0 || lk <= 0 || dim != FA_D)
     return (int)cudaErrorInvalidValue;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (!out && !oq) || (oq && !os)) return (int)cudaErrorInvalidValue;
   if (out && !aligned16(out)) return (int)cudaErrorInvalidValue;
@@ -336,6 +335,8 @@ static int attention_launch(const void* q, const void* k, const void* v, const v
   p.oq = static_cast<uint8_t*>(oq);
   p.os = static_cast<__half*>(os);
   p.oq_bytes = oq_bytes ? 1 : 0;
+  // an odd GQA group cannot pair two heads on one KV head: pair two Q tiles
+  p.qpair = (heads / kvheads) % 2 ? 1 : 0;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -345,7 +346,8 @@ static int attention_launch(const void* q, const void* k, const void* v, const v
     if (e != cudaSuccess) return (int)e;
     attr_set[dev] = true;
   }
-  dim3 grid((lq + FA_BM - 1) / FA_BM, heads / 2, batch);
+  dim3 grid(p.qpair ? (lq + 2 * FA_BM - 1) / (2 * FA_BM) : (lq + FA_BM - 1) / FA_BM, p.qpair ? heads : heads / 2,
+            batch);
   attention_kernel<<<grid, FA_THREADS, FA_SMEM_BYTES, st>>>(maps, p);
   return launch_status();
 }

@@ -40,6 +40,23 @@ def test_attention_small(cuda, B, Hq, Hkv, L):
     _check(bits(out), O.attention(q, k, v))
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,L,Lk", [(1, 4, 4, 300, 300), (2, 3, 1, 129, 129), (7, 2, 2, 40, 40),
+                                          (1, 20, 20, 98, 98), (1, 6, 2, 257, 500)])
+def test_attention_odd_group(cuda, B, Hq, Hkv, L, Lk):
+    """Odd GQA groups (group 1 is the text-fusion blocks' H20/KV20): each CTA
+    pairs two Q tiles of one head on every K/V tile."""
+    import torch
+    from k2b import ops
+
+    q, k, v = _qkv_bits(B, Hq, Hkv, L, Lk, 40 + Hq + L)
+    rng = np.random.default_rng(41)
+    gate = O.bf16_bits(rng.normal(0, 1, (B, L, Hq * 128)).astype(np.float32))
+    out = ops.attention(t_bf16(q, cuda), t_bf16(k, cuda), t_bf16(v, cuda), gate=t_bf16(gate, cuda),
+                        gate_is_sigmoid=False)
+    torch.cuda.synchronize()
+    _check(bits(out), O.attention(q, k, v, gate=gate, gate_is_sigmoid=False))
+
+
 def test_attention_cross_length_and_gate(cuda):
     import torch
     from k2b import ops
