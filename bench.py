@@ -637,7 +637,7 @@ def main():
     finite = bool(torch.isfinite(out_host.float()).all())
 
     # ------------------------------------------- config 3 (4050 tok, batch 1)
-    fwd4050 = None
+    fwd4050 = dit_ms = dit_finite = None
     if world == 1:
         from k2b.model import rope_positions, rope_table
 
@@ -666,6 +666,29 @@ def main():
         torch.cuda.synchronize()
         fwd4050 = s3.elapsed_time(e3) / args.steps
         del m3, x3, x3w
+        # the whole DiT forward around the same 28 blocks (k2b.dit): patch
+        # embedding, timestep MLP, 4 W4A4 text-fusion blocks (H20/KV20) over
+        # the 98 text tokens, the blocks, the final norm + projection;
+        # latent 16 x 152 x 104 -> 76 x 52 image tokens
+        from k2b.dit import DiTConfig, Krea2DiT, synthetic_dit
+
+        dcfg = DiTConfig(core=cfg)
+        dit = Krea2DiT(dcfg, synthetic_dit(dcfg, batch=1, seed=3, device=dev, blocks=b3))
+        g3 = torch.Generator(device=dev).manual_seed(11)
+        xl = torch.randn((1, dcfg.channels, 152, 104), generator=g3, device=dev).to(torch.bfloat16)
+        ctx = torch.randn((1, 98, dcfg.txtdim), generator=g3, device=dev).to(torch.bfloat16)
+        tsv = torch.full((1,), 0.5, device=dev)
+        for _ in range(args.warmup):
+            dit.forward(xl, tsv, ctx)
+        torch.cuda.synchronize()
+        s3.record()
+        for _ in range(args.steps):
+            yl = dit.forward(xl, tsv, ctx)
+        e3.record()
+        torch.cuda.synchronize()
+        dit_ms = s3.elapsed_time(e3) / args.steps
+        dit_finite = bool(torch.isfinite(yl.float()).all())
+        del dit, xl, ctx, yl
 
     # ------------------------------------------------------------ CPU baseline
     cpu = None
@@ -696,6 +719,10 @@ def main():
                        parallelism=par, tp=tp, dp=topo.dp, latents_per_group=local,
                        l2="inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"),
             "forward_ms_4050": fwd4050,
+            "dit_forward_ms_4050": dit_ms,
+            "dit_forward_note": "whole DiT forward at config 3 (98 text + 76x52 image tokens, 1 latent): "
+                                "patch embed, timestep MLP, 4 W4A4 text-fusion blocks (H20/KV20), 28 blocks, "
+                                "final norm + projection (k2b.dit); output finite: " + str(dit_finite),
             "e2e": {"value": e2e_value, "unit": "latents/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": x_host.numel() * 2 * world,
                     "d2h_bytes_per_step": out_host.numel() * 2 * world},

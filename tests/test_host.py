@@ -73,3 +73,27 @@ def test_e4m3_code_table_matches_torch_float8():
     pos = (0x44403800).to_bytes(4, "little") + (0x4E4C4A48).to_bytes(4, "little")
     neg = (0xCACCCED0).to_bytes(4, "little") + (0xB8C0C4C8).to_bytes(4, "little")
     assert list(pos) == list(ref[8:]) and list(neg) == list(ref[:8])
+
+
+def test_dit_patch_layout_and_helpers():
+    """k2b.dit's host-side pieces: patchify / unpatchify are inverse
+    ('b c (h ph) (w pw) <-> b (h w) (c ph pw)', graph_model.py:300-301), text
+    tokens sit at position 0 (graph_model.py:242), the identity RoPE table is
+    [[1, 0], [0, 1]] and the timestep embedding follows native_runtime.cpp:511-513."""
+    import math
+
+    import torch
+    from k2b import dit
+
+    x = torch.randn(2, 4, 6, 10)
+    t, h, w = dit.patchify(x, 2)
+    assert t.shape == (2, 15, 16) and (h, w) == (3, 5)
+    assert torch.equal(t[1, 5 + 2, 4 * 1 + 2 * 1 + 0], x[1, 1, 2 * 1 + 1, 2 * 2 + 0])
+    assert torch.equal(dit.unpatchify(t, h, w, 2, 4), x)
+    pos = dit.positions(3, 2, 4)
+    assert pos.shape == (11, 2) and not pos[:3].any() and pos[3 + 4 * 1 + 2].tolist() == [1.0, 2.0]
+    f = dit.identity_rope(5, "cpu")
+    assert torch.equal(f[2, 7], torch.tensor([[1.0, 0.0], [0.0, 1.0]]))
+    e = dit.timestep_embedding(torch.tensor([0.25]), 8)
+    args = 250.0 * torch.exp(-math.log(10000.0) * torch.arange(4, dtype=torch.float32) / 4)
+    assert torch.allclose(e[0], torch.cat([args.cos(), args.sin()]))
