@@ -141,6 +141,19 @@ struct GemmSegment {
   const float* normw;    // SEG_QKNORM: fp32 [128] ("w+1" form)
   float eps;             // SEG_QKNORM
   __half* out_scale;     // SEG_SWIGLU(_E4M3): fp16 [M, n/128]
+  // Optional LoRA bypass delta (graph_ops.py:246-249: value + T(T(x down^T)
+  // up^T) * s), applied to T(p) before the segment's epilogue:
+  // p' = T(T(p) + T(T(d) * s)), d[r, c] = sum_k lt[r, k] * lup[c, k] (fp32),
+  // lt bf16 [M, lr] = T(x down^T), lup bf16 [n, lr], lr % 8 == 0.  SwiGLU:
+  // lt/lup for the gate half, lt2/lup2 for the up half.
+  const __nv_bfloat16* lt;
+  const __nv_bfloat16* lup;
+  int lr;
+  float ls;
+  const __nv_bfloat16* lt2;
+  const __nv_bfloat16* lup2;
+  int lr2;
+  float ls2;
 };
 
 enum GemmMode : int {
@@ -193,10 +206,48 @@ __device__ __forceinline__ void store_bf16x64(__nv_bfloat16* o, const float (&v)
   }
 }
 
+// LoRA delta of 32 register slots holding consecutive columns c .. c+31 of
+// one row: acc = T(T(acc) + T(T(d) * s)), d = trow . up[c + j] in fp32.  The
+// factor rows are read with 16-byte loads that are uniform across the warp
+// (every lane of a warp covers the same columns), eight slots at a time to
+// stay inside the epilogue's register budget.
+__device__ __forceinline__ void lora_delta32(float* acc, const __nv_bfloat16* __restrict__ trow,
+                                             const __nv_bfloat16* __restrict__ up, int r, float s) {
+#pragma unroll
+  for (int h = 0; h < 32; h += 8) {
+    float d[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = 0.0f;
+    for (int k = 0; k < r; k += 8) {
+      const uint4 t4 = __ldg(reinterpret_cast<const uint4*>(trow + k));
+      const __nv_bfloat162* t2 = reinterpret_cast<const __nv_bfloat162*>(&t4);
+      float2 tf[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tf[e] = __bfloat1622float2(t2[e]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 u4 = __ldg(reinterpret_cast<const uint4*>(up + (int64_t)(h + j) * r + k));
+        const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&u4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 uf = __bfloat1622float2(u2[e]);
+          d[j] = __fmaf_rn(tf[e].x, uf.x, d[j]);
+          d[j] = __fmaf_rn(tf[e].y, uf.y, d[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      acc[h + j] = bf16_round(__fadd_rn(bf16_round(acc[h + j]), bf16_round(__fmul_rn(bf16_round(d[j]), s))));
+  }
+}
+
 // PAIRW: SwiGLU launches (one segment of gate/up column pairs); the column
 // mapping of the epilogue threads is then a compile-time choice.  MODE: a
-// GemmMode (operand forms and scale contract).
-template <bool PAIRW, int MODE>
+// GemmMode (operand forms and scale contract).  LORA: the variant that
+// applies the segments' LoRA deltas (its code stays out of the others'
+// register allocation).
+template <bool PAIRW, int MODE, bool LORA = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w4a4_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ WeightMaps wmaps,
                      const __grid_constant__ GemmParams p) {
@@ -613,6 +664,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         acc[2 * j + 1] = acc2[j].y;
       }
 
+    }
+    // LoRA bypass deltas (the slots hold consecutive columns: 64 from
+    // n0 + 64 cq, or 32 gate + 32 up columns from n0 + 32 cq for SwiGLU)
+    if (LORA && ok && row_ok && (S.lt || S.lt2)) {
+      const int c0 = n0 + ca;
+      if (pairw) {
+        if (S.lt) lora_delta32(acc, S.lt + (int64_t)row * S.lr, S.lup + (int64_t)c0 * S.lr, S.lr, S.ls);
+        if (S.lt2)
+          lora_delta32(acc + 32, S.lt2 + (int64_t)row * S.lr2, S.lup2 + (int64_t)c0 * S.lr2, S.lr2, S.ls2);
+      } else if (S.lt && c0 < S.n) {
+        lora_delta32(acc, S.lt + (int64_t)row * S.lr, S.lup + (int64_t)c0 * S.lr, S.lr, S.ls);
+        lora_delta32(acc + 32, S.lt + (int64_t)row * S.lr, S.lup + (int64_t)(c0 + 32) * S.lr, S.lr, S.ls);
+      }
     }
     // ---------------------------------------------------- final epilogue
     // CTA-uniform decision: every epilogue warp reaches this barrier, then all

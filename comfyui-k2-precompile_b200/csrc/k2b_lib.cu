@@ -146,6 +146,16 @@ struct SegDesc {
   void* out_scale;
   const void* w2;         // SwiGLU: up projection, prepared s8 [n, K]
   const void* wscale2;    // SwiGLU: fp32 [K/128, n]
+  // optional LoRA bypass factors (GemmSegment::lt ...): lt bf16 [M, lr],
+  // lup bf16 [n, lr], strength ls; lt2 / lup2 / lr2 / ls2 for SwiGLU's up half
+  const void* lt = nullptr;
+  const void* lup = nullptr;
+  int lr = 0;
+  float ls = 0.0f;
+  const void* lt2 = nullptr;
+  const void* lup2 = nullptr;
+  int lr2 = 0;
+  float ls2 = 0.0f;
 };
 
 // Reference-contract arguments of gemm_launch (GM_REF* modes): activation
@@ -211,6 +221,21 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
     g.normw = d.normw;
     g.eps = d.eps;
     g.out_scale = static_cast<__half*>(d.out_scale);
+    auto lora_ok = [](const void* t, const void* up, int r) {
+      return (t == nullptr && up == nullptr) ||
+             (t && up && aligned16(t) && aligned16(up) && r > 0 && r % 8 == 0 && r <= 1024);
+    };
+    if (!lora_ok(d.lt, d.lup, d.lr) || !lora_ok(d.lt2, d.lup2, d.lr2) || (d.lt2 && !pairw) ||
+        ((d.lt || d.lt2) && (d.kind == SEG_F32 || d.kind == SEG_F32_SCATTER)))
+      return (int)cudaErrorInvalidValue;
+    g.lt = static_cast<const __nv_bfloat16*>(d.lt);
+    g.lup = static_cast<const __nv_bfloat16*>(d.lup);
+    g.lr = d.lr;
+    g.ls = d.ls;
+    g.lt2 = static_cast<const __nv_bfloat16*>(d.lt2);
+    g.lup2 = static_cast<const __nv_bfloat16*>(d.lup2);
+    g.lr2 = d.lr2;
+    g.ls2 = d.ls2;
     if (d.kind == SEG_QKNORM && (!d.normw || !freqs || !aligned16(freqs))) return (int)cudaErrorInvalidValue;
     if (d.kind == SEG_RESIDUAL && (!gate || !resid || !aligned16(gate) || !aligned16(resid) || d.ld % 8))
       return (int)cudaErrorInvalidValue;
@@ -264,10 +289,20 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
       {gemm_w4a4_kernel<false, GM_REF4>, gemm_w4a4_kernel<true, GM_REF4>},
       {gemm_w4a4_kernel<false, GM_REF8>, nullptr},
       {gemm_w4a4_kernel<false, GM_REFF8>, nullptr}};
-  if (mode < 0 || mode > GM_REFF8 || !kernels[mode][pairw ? 1 : 0]) return (int)cudaErrorInvalidValue;
-  GemmKernel kern = kernels[mode][pairw ? 1 : 0];
-  const int variant = 2 * mode + (pairw ? 1 : 0);
-  static bool attr_set[64][10] = {};
+  // LoRA variants: the group-128 packed-A and the reference INT4 contracts
+  static const GemmKernel lora_kernels[5][2] = {
+      {gemm_w4a4_kernel<false, GM_PACKED, true>, gemm_w4a4_kernel<true, GM_PACKED, true>},
+      {nullptr, nullptr},
+      {gemm_w4a4_kernel<false, GM_REF4, true>, gemm_w4a4_kernel<true, GM_REF4, true>},
+      {nullptr, nullptr},
+      {nullptr, nullptr}};
+  bool lora = false;
+  for (int i = 0; i < nseg; ++i) lora = lora || segs[i].lt || segs[i].lt2;
+  if (mode < 0 || mode > GM_REFF8) return (int)cudaErrorInvalidValue;
+  GemmKernel kern = (lora ? lora_kernels : kernels)[mode][pairw ? 1 : 0];
+  if (!kern) return (int)cudaErrorInvalidValue;
+  const int variant = 10 * (lora ? 1 : 0) + 2 * mode + (pairw ? 1 : 0);
+  static bool attr_set[64][20] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
@@ -762,6 +797,60 @@ K2B_EXPORT int k2b_ref_gated_residual(const void* a, const void* xs, const void*
   r.xs = static_cast<const float*>(xs);
   return gemm_launch(a, nullptr, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0,
                      0, GM_REF4, &r);
+}
+
+// ------------------------------------------------------ LoRA bypass deltas
+// A projection with one LoRA bypass factor pair fused into its epilogue
+// (graph_ops.py:246-249 composes value + T(T(x down^T) up^T) * s after the
+// projection):  out = E(T(T(p) + T(T(t up^T) * s))), t = T(x down^T) bf16
+// [m, lr] (the caller's rank-lr product of the bf16 input), up bf16 [n, lr],
+// lr % 8 == 0; E = T (gate and residual null) or the gated residual
+// T(residual + T(p' * gate[row / length])).
+//   contract 0: group-128 W4A4 (a packed [m, k/2], s fp16 [m, k/128], w / ws
+//               prepared); contract 1: the reference's INT4 (a packed, s fp32
+//               [m], w packed [n, k/2], ws fp32 [n]; bias fp32 [n] or null).
+K2B_EXPORT int k2b_lora_gemm(int contract, const void* a, const void* s, const void* w, const void* ws,
+                             const void* bias, const void* gate, const void* residual, int length, const void* lt,
+                             const void* lup, int lr, float ls, void* out, int m, int n, int k, void* stream) {
+  if ((contract != 0 && contract != 1) || !lt || !lup || (gate == nullptr) != (residual == nullptr) ||
+      (bias && (contract != 1 || gate)) || length <= 0)
+    return (int)cudaErrorInvalidValue;
+  SegDesc d = {gate ? SEG_RESIDUAL : SEG_BF16, n, w, ws, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  d.lt = lt;
+  d.lup = lup;
+  d.lr = lr;
+  d.ls = ls;
+  if (contract == 0)
+    return gemm_launch(a, s, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream);
+  RefScales r;
+  r.xs = static_cast<const float*>(s);
+  r.bias = static_cast<const float*>(bias);
+  return gemm_launch(a, nullptr, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0,
+                     0, GM_REF4, &r);
+}
+
+// SwiGLU with a LoRA pair on each half: h = T(T(silu(g')) * u'), g' / u' the
+// LoRA-corrected T(p) of the gate / up projections (either pair may be null),
+// bf16 h [m, width]; contract as k2b_lora_gemm.
+K2B_EXPORT int k2b_lora_swiglu(int contract, const void* a, const void* s, const void* wg, const void* sg,
+                               const void* wu, const void* su, const void* lt_g, const void* lup_g, int lr_g,
+                               float ls_g, const void* lt_u, const void* lup_u, int lr_u, float ls_u, void* h,
+                               int m, int width, int k, void* stream) {
+  if ((contract != 0 && contract != 1) || width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU_BF16, width, wg, sg, h, width, nullptr, 0.0f, nullptr, wu, su};
+  d.lt = lt_g;
+  d.lup = lup_g;
+  d.lr = lr_g;
+  d.ls = ls_g;
+  d.lt2 = lt_u;
+  d.lup2 = lup_u;
+  d.lr2 = lr_u;
+  d.ls2 = ls_u;
+  if (contract == 0) return gemm_launch(a, s, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+  RefScales r;
+  r.xs = static_cast<const float*>(s);
+  return gemm_launch(a, nullptr, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                     GM_REF4, &r);
 }
 
 #include "abi_reference.cuh"

@@ -61,6 +61,8 @@ SIGNATURES = {
     "k2b_shim_status": (_I, [_I]),
     "k2_quant8": (None, [_P] * 3 + [ctypes.c_int64] * 2 + [_I, _I, _P]),
     "k2b_gemm8": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _P]),
+    "k2b_lora_gemm": (_I, [_I] + [_P] * 7 + [_I, _P, _P, _I, _F, _P, _I, _I, _I, _P]),
+    "k2b_lora_swiglu": (_I, [_I] + [_P] * 8 + [_I, _F, _P, _P, _I, _F, _P, _I, _I, _I, _P]),
     "k2b_gemm_f8": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P]),
     "k2b_ref_qkv": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
     "k2b_ref_gated_residual": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),

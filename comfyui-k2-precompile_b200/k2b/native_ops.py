@@ -31,9 +31,10 @@ from __future__ import annotations
 import math
 import threading
 from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
+import torch.nn.functional as F
 
 from . import ops, ref_ops
 
@@ -82,6 +83,7 @@ class Binding:
     optimize_io: bool
     weight: Optional[ops.PreparedWeight] = None
     ref: Optional[RefWeight] = None
+    loras: List[Tuple[torch.Tensor, torch.Tensor, float]] = field(default_factory=list)
     tensors: List[torch.Tensor] = field(default_factory=list)
     lookahead: List[int] = field(default_factory=list)
     routes: Dict[int, int] = field(default_factory=dict)
@@ -198,6 +200,33 @@ def add_binding(key: int, kind: int, format: int, cpu: Sequence[torch.Tensor], g
         raise ValueError(f"unknown binding kind {kind}")
     with _lock:
         _records[b.key] = b
+
+
+def set_loras(key: int, factors: Sequence[Tuple[torch.Tensor, torch.Tensor, float]]) -> None:
+    """Attach LoRA bypass factors to projection ``key``: (up [N, r], down
+    [r, K], strength), as NativePlan.register collects them from ComfyUI's
+    bypass hooks (native_schedule.py:169-182; strength = alpha / r *
+    multiplier).  The reference applies them after its native projection in
+    Python (graph_ops.py:246-249: value + T(T(x down^T) up^T) * s, one factor
+    after the other); here the first factor's up-projection is fused into the
+    projection's epilogue (``k2b_lora_gemm``) and any further ones follow in
+    that order.  Ops on bindings with factors take the per-projection routes,
+    as the reference's graph does for them (graph_ops.py:439, 501, 520).  An
+    empty list removes the factors.  Only a caller that does not also apply
+    them itself should attach them."""
+    b = _proj(key)
+    n, K = _width(b), (b.weight.k if b.weight is not None else b.ref.k)
+    out = []
+    for up, down, strength in factors:
+        r = int(down.shape[0])
+        if tuple(up.shape) != (n, r) or tuple(down.shape) != (r, K):
+            raise ValueError(f"LoRA factors must be up [{n}, r] and down [r, {K}]")
+        rp = -(-r // 8) * 8  # zero-padded rank (zero columns add nothing)
+        u = _pad_rows_cols(up.to(torch.bfloat16), n, rp)
+        d = _pad_rows_cols(down.to(torch.bfloat16), rp, K)
+        out.append((u, d, float(strength)))
+    with _lock:
+        b.loras = out
 
 
 def release_bindings(keys: Sequence[int]) -> None:
@@ -369,6 +398,8 @@ def _linear(x: torch.Tensor, key: int, gate: Optional[torch.Tensor] = None,
     """native_runtime.cpp:325-332: one projection, optionally
     out = T(residual + T(T(p) * gate)) (fused into the GEMM for INT4)."""
     b = _proj(key)
+    if b.loras:
+        return _linear_lora(x, b, gate, residual)
     if b.weight is not None:
         return _linear_gated(x, key, gate, residual)
     r = b.ref
@@ -393,10 +424,57 @@ def _linear(x: torch.Tensor, key: int, gate: Optional[torch.Tensor] = None,
     return ops.elementwise(gate.contiguous(), out.contiguous(), residual.contiguous(), 2, int(gate.numel()))
 
 
+def _linear_lora(x: torch.Tensor, b: Binding, gate: Optional[torch.Tensor], residual: Optional[torch.Tensor]):
+    """A projection with LoRA bypass factors (graph_ops.py:246-249): the first
+    factor pair's up-projection runs in the projection's epilogue (and with a
+    single factor the gated residual too); t = T(x down^T) is the rank-r
+    product of the bf16 input, a plain library GEMM as in the reference."""
+    rows, length, K = _rows_len(x)
+    x2 = x.reshape(rows, K).contiguous()
+    n = _width(b)
+    up0, down0, s0 = b.loras[0]
+    t0 = F.linear(x2, down0)
+    fuse_gate = gate is not None and len(b.loras) == 1
+    g = None
+    if fuse_gate:
+        g = gate.reshape(-1, n).contiguous()
+        if g.shape[0] == 1 and rows // length > 1:
+            g = g.expand(rows // length, n).contiguous()
+        res = residual.reshape(rows, n).contiguous()
+    r = b.ref
+    if b.weight is not None:
+        a, sa = ops.rotate_quant(x2)
+        out = ops.lora_gemm(a, sa, b.weight, t0, up0, s0, g if fuse_gate else None, res if fuse_gate else None,
+                            length=length)
+    elif r.format == 1 and not r.padded and not (fuse_gate and r.bias is not None):
+        qa, qs = ref_ops.quant4(x2, r.group)
+        out = ref_ops.lora_gemm4(qa, qs.reshape(-1), r.w, r.ws, t0, up0, s0, r.bias, g if fuse_gate else None,
+                                 res if fuse_gate else None, length=length)
+    else:
+        out = _ref_project(x2, r) + F.linear(t0, up0) * s0
+        fuse_gate = False
+    for up, down, st in b.loras[1:]:
+        out = out + F.linear(F.linear(x2, down), up) * st
+    b.count("lora_gemm")
+    if fuse_gate:
+        return out.reshape(residual.shape)
+    out = out.reshape(list(x.shape[:-1]) + [n])
+    return out if gate is None else residual + gate * out
+
+
+def _no_lora(bs: Sequence[Binding]) -> None:
+    """The prepared-input ops receive only the packed normalised activation
+    (x is metadata, input_quant_ops.py:23-31): a LoRA delta needs the bf16
+    input, so bindings with factors are refused there rather than run without
+    them (the reference's graph routes such projections per module)."""
+    if any(b.loras for b in bs):
+        raise RuntimeError("LoRA factors need the bf16 input: use joint_qkv / joint_swiglu / managed for these keys")
+
+
 def _all_int4(bs: Sequence[Binding]) -> bool:
     g = bs[0].group
     return all(b.ref is not None and b.format == 1 and b.group == g and b.ref.bias is None and not b.ref.padded
-               for b in bs)
+               and not b.loras for b in bs)
 
 
 def _group(x: torch.Tensor, keys: Sequence[int], prepared=None) -> List[torch.Tensor]:
@@ -408,6 +486,9 @@ def _group(x: torch.Tensor, keys: Sequence[int], prepared=None) -> List[torch.Te
     outs = []
     for i, key in enumerate(keys):
         b = _proj(key)
+        if b.loras:
+            outs.append(_linear(x, key).reshape(rows, -1))
+            continue
         if b.weight is not None:
             if ("b128",) not in cache:
                 cache[("b128",)] = ops.rotate_quant(x2) if prepared is None else prepared
@@ -544,6 +625,7 @@ def _residual_norm(x, gate, residual, scale, shift, key, norm_key):
 def _qkv_prepared(x, qa, qs, freqs, keys, norms, heads, kvheads):
     bs = [_proj(k) for k in keys]
     bs[0].count("prepared_qkv")
+    _no_lora(bs)
     if qs.dtype == torch.float32:
         a, s = _ref_prepared(x, qa, qs, keys)
         if _all_int4(bs):
@@ -556,6 +638,8 @@ def _qkv_prepared(x, qa, qs, freqs, keys, norms, heads, kvheads):
 def _joint_qkv(x, freqs, keys, norms, heads, kvheads):
     bs = [_proj(k) for k in keys]
     rows, _, K = _rows_len(x)
+    if any(b.loras for b in bs):
+        return _split_qkv(x, keys, norms, freqs, heads, kvheads)
     if all(b.weight is not None for b in bs):
         a, s = ops.rotate_quant(x.reshape(rows, K).contiguous())
         bs[0].count("joint_qkv")
@@ -566,6 +650,23 @@ def _joint_qkv(x, freqs, keys, norms, heads, kvheads):
         return _ref_qkv(x, a, s, freqs, keys, norms, heads, kvheads)
     bs[0].count("routed_qkv_split")
     return _split_qkv(x, keys, norms, freqs, heads, kvheads)
+
+
+def _swiglu_lora(x, keys, width):
+    """SwiGLU over bindings with LoRA factors: with group-128 weights and at
+    most one factor pair each, both deltas run in the SwiGLU GEMM's epilogue;
+    otherwise the per-projection route of the reference (graph_model.py:15-19)."""
+    wg, wu = _proj(keys[0]), _proj(keys[1])
+    rows, _, K = _rows_len(x)
+    shape = list(x.shape[:-1]) + [width]
+    if wg.weight is not None and wu.weight is not None and len(wg.loras) <= 1 and len(wu.loras) <= 1:
+        x2 = x.reshape(rows, K).contiguous()
+        a, s = ops.rotate_quant(x2)
+        lo = [None if not b.loras else (F.linear(x2, b.loras[0][1]), b.loras[0][0], b.loras[0][2]) for b in (wg, wu)]
+        wg.count("lora_swiglu")
+        return ops.lora_swiglu(a, s, wg.weight, wu.weight, lo[0], lo[1]).reshape(shape)
+    pg, pu = _group(x, keys)
+    return ops.elementwise(pg.contiguous(), pu.contiguous(), None, 0).reshape(shape)
 
 
 def _swiglu_common(x, a, s, keys, width):
@@ -582,6 +683,7 @@ def _swiglu_common(x, a, s, keys, width):
 
 def _swiglu_prepared(x, qa, qs, keys, width):
     _proj(keys[0]).count("prepared_swiglu")
+    _no_lora([_proj(k) for k in keys])
     if qs.dtype == torch.float32:
         a, s = _ref_prepared(x, qa, qs, keys)
     else:
@@ -593,6 +695,8 @@ def _joint_swiglu(x, keys, width):
     rows, _, K = _rows_len(x)
     bs = [_proj(k) for k in keys]
     x2 = x.reshape(rows, K).contiguous()
+    if any(b.loras for b in bs):
+        return _swiglu_lora(x, keys, width)
     if all(b.weight is not None for b in bs):
         a, s = ops.rotate_quant(x2)
     elif _all_int4(bs):
@@ -622,6 +726,8 @@ def _attention_inputs(x, freqs, keys, widths, norms, heads, kvheads):
         outs = _project_many(x, keys, widths)
         return outs[0], outs[1], outs[2], outs[3]
     bs = [_proj(k) for k in keys]
+    if any(b.loras for b in bs):
+        return _split_qkv(x, keys, norms, freqs, heads, kvheads, sigmoid_gate=False)
     if freqs is not None and all(b.weight is not None for b in bs):
         rows, _, K = _rows_len(x)
         a, s = ops.rotate_quant(x.reshape(rows, K).contiguous())
@@ -802,5 +908,5 @@ def _kohaku_fa_fake(q, k, v, mask, gate, gate_is_sigmoid):
     return torch.empty((q.shape[0], q.shape[2], q.shape[1] * q.shape[3]), device=q.device, dtype=q.dtype)
 
 
-__all__ = ["Binding", "RefWeight", "add_binding", "release_bindings", "configure", "configure_joint", "configure_norm_quant",
+__all__ = ["Binding", "RefWeight", "add_binding", "set_loras", "release_bindings", "configure", "configure_joint", "configure_norm_quant",
            "set_route", "finish_tuning", "set_lookahead", "reset_stats", "stats", "kohaku_fa", "SCHEMAS"]

@@ -414,6 +414,58 @@ def attention_quant(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     return oq, os_
 
 
+# ------------------------------------------------------------ LoRA deltas
+
+def _lora_args(t: torch.Tensor, up: torch.Tensor, m: int, n: int):
+    _need(t.dtype == torch.bfloat16 and up.dtype == torch.bfloat16, "lora: bf16 factors expected")
+    r = int(t.shape[-1])
+    _need(tuple(t.shape) == (m, r) and tuple(up.shape) == (n, r) and r % 8 == 0 and 0 < r <= 1024,
+          "lora: t [m, r], up [n, r] with r a multiple of 8 (<= 1024)")
+    return r
+
+
+def lora_gemm(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, t: torch.Tensor, up: torch.Tensor,
+              strength: float, gate: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, *,
+              length: Optional[int] = None) -> torch.Tensor:
+    """Group-128 W4A4 projection with one LoRA pair in its epilogue:
+    p' = T(T(p) + T(T(t up^T) * s)), t = T(x down^T) bf16 [m, r]; returns p'
+    (bf16 [m, n]) or, with gate [batch, n] and residual [m, n],
+    T(residual + T(p' * gate[row // length]))."""
+    _cuda(a, sa, W.w, W.scale, t, up, gate, residual)
+    m = _act(a, sa, W.k)
+    r = _lora_args(t, up, m, W.n)
+    _need((gate is None) == (residual is None), "lora_gemm: gate and residual go together")
+    length = m if length is None else length
+    out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
+    if m == 0:
+        return out
+    check(lib().k2b_lora_gemm(0, _p(a), _p(sa), _p(W.w), _p(W.scale), None, _p(gate), _p(residual), length, _p(t),
+                              _p(up), r, ctypes.c_float(strength), _p(out), m, W.n, W.k, _stream()), "k2b_lora_gemm")
+    return out
+
+
+def lora_swiglu(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: PreparedWeight, lora_g=None,
+                lora_u=None) -> torch.Tensor:
+    """SwiGLU h = T(T(silu(g')) * u') with a LoRA pair (t, up, s) on either
+    projection (g', u' as in lora_gemm); bf16 h [m, width]."""
+    _cuda(a, sa, wg.w, wu.w)
+    m = _act(a, sa, wg.k)
+    args = []
+    for lo in (lora_g, lora_u):
+        if lo is None:
+            args += [None, None, 0, ctypes.c_float(0.0)]
+        else:
+            t, up, st = lo
+            _cuda(t, up)
+            args += [_p(t), _p(up), _lora_args(t, up, m, wg.n), ctypes.c_float(st)]
+    h = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
+    if m == 0:
+        return h
+    check(lib().k2b_lora_swiglu(0, _p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), *args, _p(h), m,
+                                wg.n, wg.k, _stream()), "k2b_lora_swiglu")
+    return h
+
+
 # ------------------------------------------------------- e4m3 byte containers
 # The block loop keeps INT4 codes between its kernels as e4m3 bytes [rows, K]
 # (one byte per code, column order): its GEMMs then load A with TMA straight

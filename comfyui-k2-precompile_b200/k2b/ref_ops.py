@@ -239,3 +239,23 @@ def gated_residual(a: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch
         check(lib().k2b_ref_gated_residual(_p(a), _p(xs), _p(w), _p(ws), _p(gate), _p(residual), _p(out), m, length,
                                            n, k, _stream()), "k2b_ref_gated_residual")
     return out
+
+
+def lora_gemm4(a: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor, t: torch.Tensor,
+               up: torch.Tensor, strength: float, bias: Optional[torch.Tensor] = None,
+               gate: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, *,
+               length: Optional[int] = None) -> torch.Tensor:
+    """k2_gemm4 (or the gated residual) with one LoRA pair in the epilogue:
+    p' = T(T(acc * xs * ws [+ bias]) + T(T(t up^T) * s))."""
+    from .ops import _lora_args
+
+    _cuda(a, xs, w, ws, t, up, bias, gate, residual)
+    m, n, k = _proj_shapes(a, xs, w, ws, True)
+    r = _lora_args(t, up, m, n)
+    _need((gate is None) == (residual is None) and (bias is None or gate is None), "lora_gemm4: arguments")
+    length = m if length is None else length
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    if m:
+        check(lib().k2b_lora_gemm(1, _p(a), _p(xs), _p(w), _p(ws), _p(bias), _p(gate), _p(residual), length, _p(t),
+                                  _p(up), r, ctypes.c_float(strength), _p(out), m, n, k, _stream()), "k2b_lora_gemm")
+    return out

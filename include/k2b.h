@@ -252,6 +252,24 @@ int k2b_ref_qkv(const void* a, const void* xs, const void* wq, const void* sq, c
 int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const void* ws, const void* gate,
                            const void* residual, void* out, int m, int length, int n, int k, void* stream);
 
+/* ------------------------------------------------------ LoRA bypass deltas --
+ * One LoRA bypass factor pair fused into a projection's epilogue (the
+ * reference composes value + T(T(x down^T) up^T) * s after the projection,
+ * graph_ops.py:246-249; native_schedule.py:169-182 collects the factors):
+ * out = E(T(T(p) + T(T(t up^T) * s))), t bf16 [m, lr] = T(x down^T), up bf16
+ * [n, lr], lr % 8 == 0 and <= 1024; E = T, or the gated residual
+ * T(residual + T(p' * gate[row / length])) when gate and residual are given.
+ * contract 0: group-128 W4A4 (a packed, s fp16 [m, k/128], prepared w / ws);
+ * contract 1: the reference's INT4 (a packed, s fp32 [m], w packed [n, k/2],
+ * ws fp32 [n], bias fp32 [n] or null).  k2b_lora_swiglu: SwiGLU with a pair
+ * per half (either may be null), bf16 h [m, width]. */
+int k2b_lora_gemm(int contract, const void* a, const void* s, const void* w, const void* ws, const void* bias,
+                  const void* gate, const void* residual, int length, const void* lt, const void* lup, int lr,
+                  float ls, void* out, int m, int n, int k, void* stream);
+int k2b_lora_swiglu(int contract, const void* a, const void* s, const void* wg, const void* sg, const void* wu,
+                    const void* su, const void* lt_g, const void* lup_g, int lr_g, float ls_g, const void* lt_u,
+                    const void* lup_u, int lr_u, float ls_u, void* h, int m, int width, int k, void* stream);
+
 /* ------------------------------------------------------------ block loop --
  * Native loop over transformer blocks (replaces the compiled entry that
  * NativeGraph::run drives, native_runtime.cpp:543-571, over graph_model.py's
