@@ -8,6 +8,19 @@
 
 namespace k2b {
 
+// Packed INT4 codes (two per byte, even column in the low nibble, two's
+// complement) -> one e4m3 byte per code, the GEMMs' byte-A container.  n16
+// chunks of 16 packed bytes (32 codes); each thread turns one chunk into 32
+// contiguous output bytes, so loads and stores are coalesced.
+__global__ void expand_e4m3_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int64_t n16) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 lo, hi;
+    unpack_chunk(__ldg(in + i), lo, hi);
+    out[2 * i] = lo;
+    out[2 * i + 1] = hi;
+  }
+}
+
 // mode 0: z = bf16(silu(a)), mode 1: z = bf16(sigmoid(a)); y = b ? bf16(z*b) : z.
 // mode 2: y = bf16(r + bf16(b * a[i % width]))  (gated residual, gate row a).
 __global__ void elementwise_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,

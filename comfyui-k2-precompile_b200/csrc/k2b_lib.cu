@@ -288,11 +288,11 @@ static int gemm_launch(const void* a, const void* sa, int M, int K, const SegDes
       {gemm_w4a4_kernel<false, GM_BYTES>, gemm_w4a4_kernel<true, GM_BYTES>},
       {gemm_w4a4_kernel<false, GM_REF4>, gemm_w4a4_kernel<true, GM_REF4>},
       {gemm_w4a4_kernel<false, GM_REF8>, nullptr},
-      {gemm_w4a4_kernel<false, GM_REFF8>, nullptr}};
-  // LoRA variants: the group-128 packed-A and the reference INT4 contracts
+      {gemm_w4a4_kernel<false, GM_REFF8>, gemm_w4a4_kernel<true, GM_REFF8>}};
+  // LoRA variants: the group-128 (packed or e4m3 byte A) and the reference INT4 contracts
   static const GemmKernel lora_kernels[5][2] = {
       {gemm_w4a4_kernel<false, GM_PACKED, true>, gemm_w4a4_kernel<true, GM_PACKED, true>},
-      {nullptr, nullptr},
+      {gemm_w4a4_kernel<false, GM_BYTES, true>, gemm_w4a4_kernel<true, GM_BYTES, true>},
       {gemm_w4a4_kernel<false, GM_REF4, true>, gemm_w4a4_kernel<true, GM_REF4, true>},
       {nullptr, nullptr},
       {nullptr, nullptr}};
@@ -564,6 +564,19 @@ K2B_EXPORT int k2b_elementwise(const void* a, const void* b, const void* r, void
   return launch_status();
 }
 
+// Packed INT4 codes [rows, K/2] -> e4m3 bytes [rows, K] (nbytes = packed
+// bytes, a multiple of 16; both buffers 16-byte aligned).
+K2B_EXPORT int k2b_expand_e4m3(const void* a, void* a8, long long nbytes, void* stream) {
+  if (nbytes < 0 || nbytes % 16 || !aligned16(a) || !aligned16(a8)) return (int)cudaErrorInvalidValue;
+  if (nbytes == 0) return 0;
+  const long long n16 = nbytes / 16;
+  const long long blocks = (n16 + 255) / 256;
+  const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
+  expand_e4m3_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint4*>(a), static_cast<uint4*>(a8),
+                                                              (int64_t)n16);
+  return launch_status();
+}
+
 K2B_EXPORT int k2b_rope(const void* q, const void* k, const void* f, void* qo, void* ko, int batch, int length, int qh,
                         int kh, int dim, int fb, void* stream) {
   if (batch <= 0 || length <= 0 || qh < 0 || kh < 0 || qh + kh == 0 || dim <= 0 || dim % 2 || (fb != 1 && fb != batch))
@@ -725,6 +738,34 @@ K2B_EXPORT int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void*
   return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
 }
 
+K2B_EXPORT int k2b_gemm_bf16_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, void* out, int m,
+                                  int n, int k, void* stream) {
+  SegDesc d = {SEG_BF16, n, w, wscale, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
+}
+
+K2B_EXPORT int k2b_swiglu_quant_a8(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
+                                   const void* su, void* hq, void* hs, int m, int width, int k, void* stream) {
+  if (width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU, width, wg, sg, hq, width / 2, nullptr, 0.0f, hs, wu, su};
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
+}
+
+K2B_EXPORT int k2b_swiglu_bf16_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
+                                    const void* su, void* h, int m, int width, int k, void* stream) {
+  if (width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU_BF16, width, wg, sg, h, width, nullptr, 0.0f, nullptr, wu, su};
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_BYTES);
+}
+
+K2B_EXPORT int k2b_gemm_f32_scatter_e4m3(const void* a8, const void* sa, const void* w, const void* wscale,
+                                         void* const* peers, int tp, int rank, int chunk, int m, int n, int k,
+                                         void* stream) {
+  SegDesc d = {SEG_F32_SCATTER, n, w, wscale, peers ? peers[0] : nullptr, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  return gemm_launch(a8, sa, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, peers, tp, rank, chunk,
+                     GM_BYTES);
+}
+
 // ------------------------------------------------ INT8 / FP8 weight formats
 // Projections of checkpoints stored as INT8 or FP8 weights (the reference's
 // formats 2 and 3/4, native_runtime.cpp:271-283, 298-311), on the same pair
@@ -789,6 +830,52 @@ K2B_EXPORT int k2b_ref_qkv(const void* a, const void* xs, const void* wq, const 
                      nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_REF4, &r);
 }
 
+// The same reference-contract INT4 projections with A and W as e4m3 code
+// bytes ([m, k] from k2b_expand_e4m3, [n, k] expanded once from the packed
+// checkpoint rows): the INT4 codes are exact e4m3 values and every partial
+// sum an integer below 2^24, so the fp32 accumulator and the result are those
+// of the packed form (GM_REF4), without its in-CTA unpacking (gate/up at
+// 33792 x 16384 x 6144: the packed joint SwiGLU takes 19.2 ms).
+//   k2b_ref_qkv8 / k2b_ref_gated_residual8: as k2b_ref_qkv /
+//   k2b_ref_gated_residual; k2b_ref_swiglu8: as k2_int4_swiglu (bf16 h).
+K2B_EXPORT int k2b_ref_qkv8(const void* a8, const void* xs, const void* wq, const void* sq, const void* wk,
+                            const void* sk, const void* wv, const void* sv, const void* wg, const void* sg,
+                            const void* nq, const void* nk, const void* freq, void* qo, void* ko, void* vo, void* go,
+                            int m, int length, int qwidth, int kvwidth, int k, float eq, float ek, void* stream) {
+  if (qwidth <= 0 || kvwidth <= 0 || qwidth % 128 || kvwidth % 128 || length <= 0 || !freq)
+    return (int)cudaErrorInvalidValue;
+  SegDesc d[4] = {
+      {SEG_QKNORM, qwidth, wq, sq, qo, qwidth, static_cast<const float*>(nq), eq, nullptr, nullptr, nullptr},
+      {SEG_QKNORM, kvwidth, wk, sk, ko, kvwidth, static_cast<const float*>(nk), ek, nullptr, nullptr, nullptr},
+      {SEG_BF16, kvwidth, wv, sv, vo, kvwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+      {SEG_SIGMOID, qwidth, wg, sg, go, qwidth, nullptr, 0.0f, nullptr, nullptr, nullptr},
+  };
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  return gemm_launch(a8, nullptr, m, k, d, (wg && go) ? 4 : 3, length, static_cast<const float*>(freq), nullptr,
+                     nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0, GM_REFF8, &r);
+}
+
+K2B_EXPORT int k2b_ref_swiglu8(const void* a8, const void* wg, const void* wu, const void* xs, const void* sg,
+                               const void* su, void* out, int m, int n, int k, void* stream) {
+  if (n <= 0 || n % 128) return (int)cudaErrorInvalidValue;
+  SegDesc d = {SEG_SWIGLU_BF16, n, wg, sg, out, n, nullptr, 0.0f, nullptr, wu, su};
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  return gemm_launch(a8, nullptr, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                     GM_REFF8, &r);
+}
+
+K2B_EXPORT int k2b_ref_gated_residual8(const void* a8, const void* xs, const void* w, const void* ws,
+                                       const void* gate, const void* residual, void* out, int m, int length, int n,
+                                       int k, void* stream) {
+  SegDesc d = {SEG_RESIDUAL, n, w, ws, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
+  RefScales r;
+  r.xs = static_cast<const float*>(xs);
+  return gemm_launch(a8, nullptr, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0,
+                     0, GM_REFF8, &r);
+}
+
 K2B_EXPORT int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const void* ws, const void* gate,
                                       const void* residual, void* out, int m, int length, int n, int k,
                                       void* stream) {
@@ -807,12 +894,13 @@ K2B_EXPORT int k2b_ref_gated_residual(const void* a, const void* xs, const void*
 // lr % 8 == 0; E = T (gate and residual null) or the gated residual
 // T(residual + T(p' * gate[row / length])).
 //   contract 0: group-128 W4A4 (a packed [m, k/2], s fp16 [m, k/128], w / ws
-//               prepared); contract 1: the reference's INT4 (a packed, s fp32
-//               [m], w packed [n, k/2], ws fp32 [n]; bias fp32 [n] or null).
+//               prepared); 2: the same with a as e4m3 bytes [m, k];
+//               contract 1: the reference's INT4 (a packed, s fp32 [m], w
+//               packed [n, k/2], ws fp32 [n]; bias fp32 [n] or null).
 K2B_EXPORT int k2b_lora_gemm(int contract, const void* a, const void* s, const void* w, const void* ws,
                              const void* bias, const void* gate, const void* residual, int length, const void* lt,
                              const void* lup, int lr, float ls, void* out, int m, int n, int k, void* stream) {
-  if ((contract != 0 && contract != 1) || !lt || !lup || (gate == nullptr) != (residual == nullptr) ||
+  if (contract < 0 || contract > 2 || !lt || !lup || (gate == nullptr) != (residual == nullptr) ||
       (bias && (contract != 1 || gate)) || length <= 0)
     return (int)cudaErrorInvalidValue;
   SegDesc d = {gate ? SEG_RESIDUAL : SEG_BF16, n, w, ws, out, n, nullptr, 0.0f, nullptr, nullptr, nullptr};
@@ -820,8 +908,9 @@ K2B_EXPORT int k2b_lora_gemm(int contract, const void* a, const void* s, const v
   d.lup = lup;
   d.lr = lr;
   d.ls = ls;
-  if (contract == 0)
-    return gemm_launch(a, s, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream);
+  if (contract != 1)
+    return gemm_launch(a, s, m, k, &d, 1, length, nullptr, gate, residual, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                       contract == 2 ? GM_BYTES : GM_PACKED);
   RefScales r;
   r.xs = static_cast<const float*>(s);
   r.bias = static_cast<const float*>(bias);
@@ -836,7 +925,7 @@ K2B_EXPORT int k2b_lora_swiglu(int contract, const void* a, const void* s, const
                                const void* wu, const void* su, const void* lt_g, const void* lup_g, int lr_g,
                                float ls_g, const void* lt_u, const void* lup_u, int lr_u, float ls_u, void* h,
                                int m, int width, int k, void* stream) {
-  if ((contract != 0 && contract != 1) || width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
+  if (contract < 0 || contract > 2 || width <= 0 || width % 128) return (int)cudaErrorInvalidValue;
   SegDesc d = {SEG_SWIGLU_BF16, width, wg, sg, h, width, nullptr, 0.0f, nullptr, wu, su};
   d.lt = lt_g;
   d.lup = lup_g;
@@ -846,7 +935,9 @@ K2B_EXPORT int k2b_lora_swiglu(int contract, const void* a, const void* s, const
   d.lup2 = lup_u;
   d.lr2 = lr_u;
   d.ls2 = ls_u;
-  if (contract == 0) return gemm_launch(a, s, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+  if (contract != 1)
+    return gemm_launch(a, s, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0,
+                       contract == 2 ? GM_BYTES : GM_PACKED);
   RefScales r;
   r.xs = static_cast<const float*>(s);
   return gemm_launch(a, nullptr, m, k, &d, 1, m, nullptr, nullptr, nullptr, (cudaStream_t)stream, nullptr, 0, 0, 0,

@@ -66,6 +66,9 @@ SIGNATURES = {
     "k2b_gemm_f8": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P]),
     "k2b_ref_qkv": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
     "k2b_ref_gated_residual": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
+    "k2b_ref_qkv8": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
+    "k2b_ref_swiglu8": (_I, [_P] * 7 + [_I, _I, _I, _P]),
+    "k2b_ref_gated_residual8": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
     "k2_gemm4": (None, [_P] * 6 + [ctypes.c_int64] * 3 + [_I, _P]),
     "k2_dequant8": (None, [_P] * 5 + [ctypes.c_int64] * 3 + [_I, _P]),
     "k2_fp8": (None, [_P, _P, _P, ctypes.c_int64, _I, _I, ctypes.c_bool, _P]),
@@ -75,6 +78,11 @@ SIGNATURES = {
     "k2b_qkv_e4m3": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
     "k2b_gated_residual_e4m3": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
     "k2b_swiglu_quant_e4m3": (_I, [_P] * 8 + [_I, _I, _I, _P]),
+    "k2b_gemm_bf16_e4m3": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "k2b_swiglu_bf16_e4m3": (_I, [_P] * 7 + [_I, _I, _I, _P]),
+    "k2b_swiglu_quant_a8": (_I, [_P] * 8 + [_I, _I, _I, _P]),
+    "k2b_gemm_f32_scatter_e4m3": (_I, [_P] * 5 + [_I] * 6 + [_P]),
+    "k2b_expand_e4m3": (_I, [_P, _P, ctypes.c_longlong, _P]),
 }
 
 _lib = None

@@ -63,9 +63,18 @@ class RefWeight:
     n: int
     k: int
 
+    w8_: Optional[torch.Tensor] = None
+
     @property
     def padded(self) -> bool:
         return self.format != 0 and (self.n % 128 != 0 or self.k % 128 != 0)
+
+    def codes8(self) -> torch.Tensor:
+        """Format 1: the weight codes as e4m3 bytes [np, kp], expanded from the
+        packed rows on first use and kept resident (the byte-operand GEMMs)."""
+        if self.w8_ is None:
+            self.w8_ = ref_ops.codes_e4m3(self.w)
+        return self.w8_
 
 
 @dataclass
@@ -376,7 +385,7 @@ def _ref_project(x2: torch.Tensor, r: RefWeight, q=None) -> torch.Tensor:
     qa, qs = _ref_quantize(x2, r) if q is None else q
     qa = _pad_k(qa, r)
     if r.format == 1:
-        out = ref_ops.gemm4(qa, qs.reshape(-1), r.w, r.ws, r.bias)
+        out = ref_ops.gemm_f8(ref_ops.codes_e4m3(qa), qs.reshape(-1), r.codes8(), r.ws, r.bias)
     elif r.format == 2:
         out = ref_ops.gemm8(qa, qs.reshape(-1), r.w, r.ws, r.bias)
     else:
@@ -412,8 +421,8 @@ def _linear(x: torch.Tensor, key: int, gate: Optional[torch.Tensor] = None,
             g = g.expand(rows // length, r.n).contiguous()
         qa, qs = ref_ops.quant4(x2, r.group)
         b.count("gated_gemm")
-        out = ref_ops.gated_residual(qa, qs.reshape(-1), r.w, r.ws, g, residual.reshape(rows, r.n).contiguous(),
-                                     length=length)
+        out = ref_ops.gated_residual8(ref_ops.codes_e4m3(qa), qs.reshape(-1), r.codes8(), r.ws, g,
+                                      residual.reshape(rows, r.n).contiguous(), length=length)
         return out.reshape(residual.shape)
     out = _ref_project(x2, r).reshape(shape)
     b.count("gemm")
@@ -535,9 +544,13 @@ def _ref_qkv(x, qa, qs, freqs, keys, norms, heads, kvheads, sigmoid_gate=True):
     B, L = int(x.shape[0]), int(x.shape[1])
     bs = [_proj(k) for k in keys]
     nq, nk = _norm(norms[0]), _norm(norms[1])
-    q, k, v, g = ref_ops.qkv(qa, qs.reshape(-1), [b.ref.w for b in bs], [b.ref.ws for b in bs], nq.tensors[0],
-                             nk.tensors[0], _freqs_for(freqs, L), length=L, eps_q=nq.eps, eps_k=nk.eps,
-                             sigmoid_gate=sigmoid_gate)
+    a8 = ref_ops.codes_e4m3(qa)
+    ws = [b.ref.ws for b in bs]
+    q, k, v, g = ref_ops.qkv8(a8, qs.reshape(-1), [b.ref.codes8() for b in bs[:4 if sigmoid_gate else 3]],
+                              ws[:4 if sigmoid_gate else 3], nq.tensors[0], nk.tensors[0], _freqs_for(freqs, L),
+                              length=L, eps_q=nq.eps, eps_k=nk.eps)
+    if not sigmoid_gate:
+        g = ref_ops.gemm_f8(a8, qs.reshape(-1), bs[3].ref.codes8(), ws[3])
     return (q.view(B, L, heads, HEAD_DIM).transpose(1, 2), k.view(B, L, kvheads, HEAD_DIM).transpose(1, 2),
             v.view(B, L, kvheads * HEAD_DIM), None if g is None else g.view(B, L, heads * HEAD_DIM))
 
@@ -677,7 +690,8 @@ def _swiglu_common(x, a, s, keys, width):
     if wg.weight is not None and wu.weight is not None:
         return ops.swiglu_bf16(a, s, wg.weight, wu.weight).reshape(shape)
     if _all_int4([wg, wu]):
-        return ref_ops.swiglu(a, s.reshape(-1), wg.ref.w, wg.ref.ws, wu.ref.w, wu.ref.ws).reshape(shape)
+        return ref_ops.swiglu8(ref_ops.codes_e4m3(a), s.reshape(-1), wg.ref.codes8(), wg.ref.ws, wu.ref.codes8(),
+                               wu.ref.ws).reshape(shape)
     raise RuntimeError("Joint SwiGLU weight contract changed")
 
 

@@ -254,19 +254,41 @@ def _act(a: torch.Tensor, sa: torch.Tensor, k: int) -> int:
     return int(a.shape[0])
 
 
+def expand_e4m3(a: torch.Tensor) -> torch.Tensor:
+    """Packed INT4 codes uint8 [m, k/2] -> e4m3 bytes uint8 [m, k] (k2b_expand_e4m3)."""
+    _cuda(a)
+    _need(a.dtype == torch.uint8 and a.dim() == 2 and a.numel() % 16 == 0, "expand_e4m3: packed uint8 [m, k/2]")
+    a8 = torch.empty((a.shape[0], 2 * a.shape[1]), dtype=torch.uint8, device=a.device)
+    if a.numel():
+        check(lib().k2b_expand_e4m3(_p(a), _p(a8), a.numel(), _stream()), "k2b_expand_e4m3")
+    return a8
+
+
+def _a8(a: torch.Tensor, sa: torch.Tensor, k: int):
+    """The GEMM's A operand as e4m3 bytes [m, k]: packed codes [m, k/2] are
+    expanded first (one pass over 1.5 bytes per code), byte containers are
+    used as they are.  The byte-A GEMM takes about 40% less time than the
+    in-CTA unpack of packed A."""
+    _need(a.dtype == torch.uint8 and sa.dtype == torch.float16 and a.dim() == 2,
+          "uint8 activations (packed or e4m3 bytes) + fp16 scales expected")
+    m = int(a.shape[0])
+    _need(tuple(sa.shape) == (m, k // GROUP) and a.shape[1] in (k // 2, k), "activation / weight K mismatch")
+    return (expand_e4m3(a) if a.shape[1] * 2 == k else a), m
+
+
 def gemm_f32(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, out: Optional[torch.Tensor] = None
              ) -> torch.Tensor:
     """fp32 a@W (exact group accumulation); ``out`` may be a preallocated
     [m, n] fp32 buffer (e.g. the first rows of a reduce-scatter input)."""
     _cuda(a, sa, W.w, W.scale, out)
-    m = _act(a, sa, W.k)
+    a8, m = _a8(a, sa, W.k)
     if out is None:
         out = torch.empty((m, W.n), dtype=torch.float32, device=a.device)
     _need(out.dtype == torch.float32 and out.dim() == 2 and tuple(out.shape) == (m, W.n), "gemm_f32: out shape")
     if m == 0:
         return out
-    check(lib().k2b_gemm_f32(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
-          "k2b_gemm_f32")
+    check(lib().k2b_gemm_f32_e4m3(_p(a8), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
+          "k2b_gemm_f32_e4m3")
     return out
 
 
@@ -275,22 +297,22 @@ def gemm_f32_scatter(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, peers
     row r to ``peers[r // chunk]`` (device pointers, fp32 [tp, chunk, n] each)
     in slot ``rank``."""
     _cuda(a, sa, W.w, W.scale)
-    m = _act(a, sa, W.k)
+    a8, m = _a8(a, sa, W.k)
     tp = len(peers)
     _need(1 <= tp <= 4 and 0 <= rank < tp and chunk > 0 and chunk * tp >= m, "gemm_f32_scatter: rank layout")
     arr = (ctypes.c_void_p * tp)(*[int(x) for x in peers])
-    check(lib().k2b_gemm_f32_scatter(_p(a), _p(sa), _p(W.w), _p(W.scale), arr, tp, rank, chunk, m, W.n, W.k,
-                                     _stream()), "k2b_gemm_f32_scatter")
+    check(lib().k2b_gemm_f32_scatter_e4m3(_p(a8), _p(sa), _p(W.w), _p(W.scale), arr, tp, rank, chunk, m, W.n, W.k,
+                                          _stream()), "k2b_gemm_f32_scatter_e4m3")
 
 
 def gemm_bf16(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight) -> torch.Tensor:
     _cuda(a, sa, W.w, W.scale)
-    m = _act(a, sa, W.k)
+    a8, m = _a8(a, sa, W.k)
     out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
     if m == 0:
         return out
-    check(lib().k2b_gemm_bf16(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
-          "k2b_gemm_bf16")
+    check(lib().k2b_gemm_bf16_e4m3(_p(a8), _p(sa), _p(W.w), _p(W.scale), _p(out), m, W.n, W.k, _stream()),
+          "k2b_gemm_bf16_e4m3")
     return out
 
 
@@ -302,7 +324,7 @@ def qkv(a: torch.Tensor, sa: torch.Tensor, wq: PreparedWeight, wk: PreparedWeigh
     Returns token-major bf16 (q [m, Hq*128], k [m, Hkv*128], v [m, Hkv*128],
     gate [m, Hq*128] or None)."""
     _cuda(a, sa, wq.w, wk.w, wv.w, nq, nk, freqs, None if wg is None else wg.w)
-    m = _act(a, sa, wq.k)
+    a8, m = _a8(a, sa, wq.k)
     _need(wk.k == wq.k and wv.k == wq.k and wk.n == wv.n, "qkv weight shapes")
     _need(nq.dtype == torch.float32 and nk.dtype == torch.float32 and nq.numel() == HEAD_DIM and
           nk.numel() == HEAD_DIM, "qkv: fp32 [128] q/k norm weights expected")
@@ -317,10 +339,10 @@ def qkv(a: torch.Tensor, sa: torch.Tensor, wq: PreparedWeight, wk: PreparedWeigh
         go = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
     if m == 0:
         return qo, ko, vo, go
-    check(lib().k2b_qkv(_p(a), _p(sa), _p(wq.w), _p(wq.scale), _p(wk.w), _p(wk.scale), _p(wv.w), _p(wv.scale),
-                        _p(None if wg is None else wg.w), _p(None if wg is None else wg.scale), _p(nq), _p(nk),
-                        _p(freqs), _p(qo), _p(ko), _p(vo), _p(go), m, length, wq.n, wk.n, wq.k,
-                        ctypes.c_float(eps_q), ctypes.c_float(eps_k), _stream()), "k2b_qkv")
+    check(lib().k2b_qkv_e4m3(_p(a8), _p(sa), _p(wq.w), _p(wq.scale), _p(wk.w), _p(wk.scale), _p(wv.w),
+                             _p(wv.scale), _p(None if wg is None else wg.w), _p(None if wg is None else wg.scale),
+                             _p(nq), _p(nk), _p(freqs), _p(qo), _p(ko), _p(vo), _p(go), m, length, wq.n, wk.n, wq.k,
+                             ctypes.c_float(eps_q), ctypes.c_float(eps_k), _stream()), "k2b_qkv_e4m3")
     return qo, ko, vo, go
 
 
@@ -328,42 +350,42 @@ def gated_residual(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, gate: t
                    residual: torch.Tensor, *, length: int) -> torch.Tensor:
     """out = bf16(residual + bf16(bf16(a@W) * gate[row // length]))."""
     _cuda(a, sa, W.w, gate, residual)
-    m = _act(a, sa, W.k)
+    a8, m = _a8(a, sa, W.k)
     _need(gate.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16, "gated_residual: bf16 expected")
     _need(residual.numel() == m * W.n and gate.numel() == (m // length) * W.n and m % length == 0,
           "gated_residual: shapes")
     out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
     if m == 0:
         return out
-    check(lib().k2b_gated_residual(_p(a), _p(sa), _p(W.w), _p(W.scale), _p(gate), _p(residual), _p(out), m, length,
-                                   W.n, W.k, _stream()), "k2b_gated_residual")
+    check(lib().k2b_gated_residual_e4m3(_p(a8), _p(sa), _p(W.w), _p(W.scale), _p(gate), _p(residual), _p(out), m,
+                                        length, W.n, W.k, _stream()), "k2b_gated_residual_e4m3")
     return out
 
 
 def swiglu_quant(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: PreparedWeight):
     """Gate/up + SwiGLU + H128 + INT4 -> (hq uint8 [m, F/2], hs fp16 [m, F/128])."""
     _cuda(a, sa, wg.w, wu.w)
-    m = _act(a, sa, wg.k)
+    a8, m = _a8(a, sa, wg.k)
     _need(wu.n == wg.n and wu.k == wg.k, "swiglu weight shapes")
     F = wg.n
     hq = torch.empty((m, F // 2), dtype=torch.uint8, device=a.device)
     hs = torch.empty((m, F // GROUP), dtype=torch.float16, device=a.device)
     if m == 0:
         return hq, hs
-    check(lib().k2b_swiglu_quant(_p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(hq), _p(hs), m,
-                                 F, wg.k, _stream()), "k2b_swiglu_quant")
+    check(lib().k2b_swiglu_quant_a8(_p(a8), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(hq), _p(hs),
+                                    m, F, wg.k, _stream()), "k2b_swiglu_quant_a8")
     return hq, hs
 
 
 def swiglu_bf16(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: PreparedWeight) -> torch.Tensor:
     _cuda(a, sa, wg.w, wu.w)
-    m = _act(a, sa, wg.k)
+    a8, m = _a8(a, sa, wg.k)
     _need(wu.n == wg.n and wu.k == wg.k, "swiglu weight shapes")
     h = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
     if m == 0:
         return h
-    check(lib().k2b_swiglu_bf16(_p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(h), m, wg.n,
-                                wg.k, _stream()), "k2b_swiglu_bf16")
+    check(lib().k2b_swiglu_bf16_e4m3(_p(a8), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), _p(h), m, wg.n,
+                                     wg.k, _stream()), "k2b_swiglu_bf16_e4m3")
     return h
 
 
@@ -432,14 +454,14 @@ def lora_gemm(a: torch.Tensor, sa: torch.Tensor, W: PreparedWeight, t: torch.Ten
     (bf16 [m, n]) or, with gate [batch, n] and residual [m, n],
     T(residual + T(p' * gate[row // length]))."""
     _cuda(a, sa, W.w, W.scale, t, up, gate, residual)
-    m = _act(a, sa, W.k)
+    a8, m = _a8(a, sa, W.k)
     r = _lora_args(t, up, m, W.n)
     _need((gate is None) == (residual is None), "lora_gemm: gate and residual go together")
     length = m if length is None else length
     out = torch.empty((m, W.n), dtype=torch.bfloat16, device=a.device)
     if m == 0:
         return out
-    check(lib().k2b_lora_gemm(0, _p(a), _p(sa), _p(W.w), _p(W.scale), None, _p(gate), _p(residual), length, _p(t),
+    check(lib().k2b_lora_gemm(2, _p(a8), _p(sa), _p(W.w), _p(W.scale), None, _p(gate), _p(residual), length, _p(t),
                               _p(up), r, ctypes.c_float(strength), _p(out), m, W.n, W.k, _stream()), "k2b_lora_gemm")
     return out
 
@@ -449,7 +471,7 @@ def lora_swiglu(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: Prepa
     """SwiGLU h = T(T(silu(g')) * u') with a LoRA pair (t, up, s) on either
     projection (g', u' as in lora_gemm); bf16 h [m, width]."""
     _cuda(a, sa, wg.w, wu.w)
-    m = _act(a, sa, wg.k)
+    a8, m = _a8(a, sa, wg.k)
     args = []
     for lo in (lora_g, lora_u):
         if lo is None:
@@ -461,7 +483,7 @@ def lora_swiglu(a: torch.Tensor, sa: torch.Tensor, wg: PreparedWeight, wu: Prepa
     h = torch.empty((m, wg.n), dtype=torch.bfloat16, device=a.device)
     if m == 0:
         return h
-    check(lib().k2b_lora_swiglu(0, _p(a), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), *args, _p(h), m,
+    check(lib().k2b_lora_swiglu(2, _p(a8), _p(sa), _p(wg.w), _p(wg.scale), _p(wu.w), _p(wu.scale), *args, _p(h), m,
                                 wg.n, wg.k, _stream()), "k2b_lora_swiglu")
     return h
 

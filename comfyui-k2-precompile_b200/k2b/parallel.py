@@ -402,7 +402,8 @@ class TPBlocks:
             qv = q.view(B, L, self.hq_heads, 128).transpose(1, 2)
             kv = k.view(B, L, self.kv_heads_local, 128).transpose(1, 2)
             vv = v.view(B, L, self.kv_heads_local, 128).transpose(1, 2)
-            oq, os_ = ops.attention_quant(qv, kv, vv)
+            # codes as e4m3 bytes: the out-projection loads them as they are
+            oq, os_ = ops.attention_quant_e4m3(qv, kv, vv)
             del q, k, v, qv, kv, vv
             mark(e + 4)
             if self.fused:
@@ -425,7 +426,8 @@ class TPBlocks:
             mark(e + 7)
             yield ("gather", (self.act_q, self.act_s))
             mark(e + 8)
-            hq, hs = ops.swiglu_quant(self.act_q[:rows], self.act_s[:rows], blk.wg, blk.wu)
+            # the gathered packed codes expanded once; h stays in e4m3 bytes for down
+            hq, hs = ops.swiglu_quant_e4m3(ops.expand_e4m3(self.act_q[:rows]), self.act_s[:rows], blk.wg, blk.wu)
             mark(e + 9)
             if self.fused:
                 ops.gemm_f32_scatter(hq, hs, blk.wd, self.peers.ptrs, r, c)

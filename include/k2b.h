@@ -212,7 +212,15 @@ int k2b_attention_quant(const void* q, const void* k, const void* v, void* oq, v
  * k2b_attention_quant_e4m3: k2b_attention_quant with oq8 u8 [B*lq, heads*128];
  * k2b_gemm_f32_e4m3 / k2b_qkv_e4m3 / k2b_gated_residual_e4m3: their packed
  *   twins with a8 u8 [m, k];
- * k2b_swiglu_quant_e4m3: a8 u8 [m, k] in, h8 u8 [m, width] + hs out. */
+ * k2b_swiglu_quant_e4m3: a8 u8 [m, k] in, h8 u8 [m, width] + hs out;
+ * k2b_gemm_bf16_e4m3 / k2b_swiglu_bf16_e4m3 / k2b_gemm_f32_scatter_e4m3:
+ *   likewise; k2b_swiglu_quant_a8: a8 u8 [m, k] in, packed hq [m, width/2]
+ *   + hs out (k2b_swiglu_quant's output).
+ * k2b_expand_e4m3: packed codes [rows, K/2] -> e4m3 bytes [rows, K]
+ *   (nbytes = rows*K/2, a multiple of 16).  The byte-A GEMM takes about 40%
+ *   less time than the packed-A form, which unpacks A inside the CTA (gate/up
+ *   at 33792 x 16384 x 6144: 12.0 against 19.8 ms), so a caller holding
+ *   packed codes expands them first (a pass over 1.5 bytes per code). */
 int k2b_norm_quant_e4m3(const void* x, const void* w, const void* scale, const void* shift, void* q8, void* s,
                         int rows, int K, int length, int cut, int batch, float eps, void* stream);
 int k2b_attention_quant_e4m3(const void* q, const void* k, const void* v, void* oq8, void* os, int batch, int heads,
@@ -229,6 +237,15 @@ int k2b_gated_residual_e4m3(const void* a8, const void* sa, const void* w, const
                             const void* residual, void* out, int m, int length, int n, int k, void* stream);
 int k2b_swiglu_quant_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
                           const void* su, void* h8, void* hs, int m, int width, int k, void* stream);
+int k2b_gemm_bf16_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, void* out, int m, int n,
+                       int k, void* stream);
+int k2b_swiglu_bf16_e4m3(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
+                         const void* su, void* h, int m, int width, int k, void* stream);
+int k2b_gemm_f32_scatter_e4m3(const void* a8, const void* sa, const void* w, const void* wscale, void* const* peers,
+                              int tp, int rank, int chunk, int m, int n, int k, void* stream);
+int k2b_swiglu_quant_a8(const void* a8, const void* sa, const void* wg, const void* sg, const void* wu,
+                        const void* su, void* hq, void* hs, int m, int width, int k, void* stream);
+int k2b_expand_e4m3(const void* a, void* a8, long long nbytes, void* stream);
 
 /* ------------------------------------ INT8 / FP8 weights, reference contract --
  * Projections of INT8 / FP8 checkpoint weights (the reference's formats 2 and
@@ -251,6 +268,20 @@ int k2b_ref_qkv(const void* a, const void* xs, const void* wq, const void* sq, c
                 int k, float eq, float ek, void* stream);
 int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const void* ws, const void* gate,
                            const void* residual, void* out, int m, int length, int n, int k, void* stream);
+/* The same with A and W as e4m3 code bytes (A [m, k] from k2b_expand_e4m3,
+ * W [n, k] expanded once from the packed checkpoint rows): identical results
+ * (exact integer sums in the fp32 accumulator) without the in-CTA unpacking
+ * of the packed forms.  k2b_ref_swiglu8: k2_int4_swiglu's arguments with a8,
+ * wg8, wu8.  The plain projection of this form is k2b_gemm_f8 with e4m3
+ * operands and per-row / per-channel scales. */
+int k2b_ref_qkv8(const void* a8, const void* xs, const void* wq, const void* sq, const void* wk, const void* sk,
+                 const void* wv, const void* sv, const void* wg, const void* sg, const void* nq, const void* nk,
+                 const void* freq, void* qo, void* ko, void* vo, void* go, int m, int length, int qwidth,
+                 int kvwidth, int k, float eq, float ek, void* stream);
+int k2b_ref_swiglu8(const void* a8, const void* wg, const void* wu, const void* xs, const void* sg, const void* su,
+                    void* out, int m, int n, int k, void* stream);
+int k2b_ref_gated_residual8(const void* a8, const void* xs, const void* w, const void* ws, const void* gate,
+                            const void* residual, void* out, int m, int length, int n, int k, void* stream);
 
 /* ------------------------------------------------------ LoRA bypass deltas --
  * One LoRA bypass factor pair fused into a projection's epilogue (the
@@ -260,6 +291,7 @@ int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const v
  * [n, lr], lr % 8 == 0 and <= 1024; E = T, or the gated residual
  * T(residual + T(p' * gate[row / length])) when gate and residual are given.
  * contract 0: group-128 W4A4 (a packed, s fp16 [m, k/128], prepared w / ws);
+ * contract 2: the same with a as e4m3 bytes [m, k];
  * contract 1: the reference's INT4 (a packed, s fp32 [m], w packed [n, k/2],
  * ws fp32 [n], bias fp32 [n] or null).  k2b_lora_swiglu: SwiGLU with a pair
  * per half (either may be null), bf16 h [m, width]. */

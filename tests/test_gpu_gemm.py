@@ -170,3 +170,36 @@ def test_swiglu_quant_bitexact(cuda, M, F, K):
     assert np.array_equal(bits(h), rh)
     assert np.array_equal(bits(hs), rs)
     assert np.array_equal(hq.cpu().numpy(), rq)
+
+
+def test_packed_exports_equal_the_byte_path(cuda):
+    """The packed-A C exports (A unpacked inside the CTA) and the route the op
+    wrappers take for packed codes (k2b_expand_e4m3, then the byte-A GEMM)
+    give identical bits; the expansion is the e4m3 table of the codes."""
+    import ctypes
+
+    import torch
+    from _helpers import e4m3_bytes
+    from k2b import ops
+    from k2b._native import lib
+
+    M, K, N = 300, 1024, 512
+    a, sa = packed_act(M, K, 91)
+    wq, ws = packed_weight(N, K, 92)
+    uq, us = packed_weight(N, K, 93)
+    A, SA = t_u8(a, cuda), t_f16(sa, cuda)
+    W = ops.prepare_weight(t_u8(wq, cuda), t_f16(ws, cuda))
+    U = ops.prepare_weight(t_u8(uq, cuda), t_f16(us, cuda))
+    a8 = ops.expand_e4m3(A)
+    assert np.array_equal(a8.cpu().numpy(), e4m3_bytes(a))
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    assert lib().k2b_gemm_f32(p(A), p(SA), p(W.w), p(W.scale), p(out), M, N, K, st) == 0
+    assert torch.equal(out, ops.gemm_f32(A, SA, W)) and torch.equal(out, ops.gemm_f32(a8, SA, W))
+    hq = torch.empty((M, N // 2), dtype=torch.uint8, device=cuda)
+    hs = torch.empty((M, N // 128), dtype=torch.float16, device=cuda)
+    assert lib().k2b_swiglu_quant(p(A), p(SA), p(W.w), p(W.scale), p(U.w), p(U.scale), p(hq), p(hs), M, N, K, st) == 0
+    hq2, hs2 = ops.swiglu_quant(A, SA, W, U)
+    torch.cuda.synchronize()
+    assert torch.equal(hq, hq2) and torch.equal(hs, hs2)

@@ -289,3 +289,38 @@ def test_ref_joint_kernels_agree_with_the_references_own(cuda):
     assert torch.equal(res[0][0], res[1][0])  # T(resid + T(T(p) * gate)): bit for bit
     d = (res[0][1].float() - res[1][1].float()).abs()
     assert float(d.max()) <= TOL_ABS and float((d == 0).float().mean()) > 0.95
+
+
+def test_byte_operand_forms_equal_the_packed_forms(cuda):
+    """The byte-operand forms (A and W as e4m3 code bytes: k2b_ref_qkv8,
+    k2b_ref_swiglu8, k2b_ref_gated_residual8, k2b_gemm_f8 with per-row /
+    per-channel scales) give the bits of the packed forms the reference-named
+    exports run, bias included."""
+    import torch
+    from k2b import ref_ops
+    from k2b.model import rope_positions, rope_table
+
+    m, K, L = 256, 1536, 128
+    _, a, xs = _act(m, K, 101, group=64)
+    A, XS = t_u8(a, cuda).view(torch.int8), t_f32(xs, cuda)
+    A8 = ref_ops.codes_e4m3(A)
+    W = {n: _weights(w, K, 110 + i) for i, (n, w) in enumerate((("q", 512), ("k", 256), ("v", 256), ("g", 512),
+                                                                 ("o", 384)))}
+    Wp = {n: t_u8(W[n][0], cuda).view(torch.int8) for n in W}
+    Ws = {n: t_f32(W[n][1], cuda) for n in W}
+    W8 = {n: ref_ops.codes_e4m3(Wp[n]) for n in W}
+    bias = t_f32(np.random.default_rng(120).normal(0, 0.1, 384).astype(np.float32), cuda)
+    assert torch.equal(ref_ops.gemm4(A, XS, Wp["o"], Ws["o"], bias), ref_ops.gemm_f8(A8, XS, W8["o"], Ws["o"], bias))
+    rng = np.random.default_rng(121)
+    nq, nk = (t_f32(rng.uniform(-0.1, 0.1, 128).astype(np.float32), cuda) for _ in range(2))
+    freqs = rope_table(rope_positions(2 * 8, 8, 14), (64, 64), 10000.0).to(cuda)  # [128, 64, 2, 2]
+    ks = ("q", "k", "v", "g")
+    got = ref_ops.qkv8(A8, XS, [W8[n] for n in ks], [Ws[n] for n in ks], nq, nk, freqs, length=L)
+    ref = ref_ops.qkv(A, XS, [Wp[n] for n in ks], [Ws[n] for n in ks], nq, nk, freqs, length=L)
+    assert all(torch.equal(x, y) for x, y in zip(got, ref))
+    assert torch.equal(ref_ops.swiglu8(A8, XS, W8["q"], Ws["q"], W8["g"], Ws["g"]),
+                       ref_ops.swiglu(A, XS, Wp["q"], Ws["q"], Wp["g"], Ws["g"]))
+    gate = t_bf16(O.bf16_bits(rng.normal(0, 0.5, (2, 384)).astype(np.float32)), cuda)
+    resid = t_bf16(O.bf16_bits(rng.normal(0, 1, (m, 384)).astype(np.float32)), cuda)
+    assert torch.equal(ref_ops.gated_residual8(A8, XS, W8["o"], Ws["o"], gate, resid, length=L),
+                       ref_ops.gated_residual(A, XS, Wp["o"], Ws["o"], gate, resid, length=L))
