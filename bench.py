@@ -637,7 +637,7 @@ def main():
     finite = bool(torch.isfinite(out_host.float()).all())
 
     # ------------------------------------------- config 3 (4050 tok, batch 1)
-    fwd4050 = dit_ms = dit_finite = None
+    fwd4050 = dit_ms = dit_finite = ref_contract_ms = ref_contract_finite = None
     if world == 1:
         from k2b.model import rope_positions, rope_table
 
@@ -689,6 +689,23 @@ def main():
         dit_ms = s3.elapsed_time(e3) / args.steps
         dit_finite = bool(torch.isfinite(yl.float()).all())
         del dit, xl, ctx, yl
+        # the same 28-block forward in the reference's own contract (a ConvRot
+        # W4A4 checkpoint's arithmetic: ConvRot 256, one fp32 scale per row and
+        # per channel, the attention gate, joint kernels; k2b.ref_blocks)
+        from k2b.ref_blocks import ref_forward, synthetic_ref_blocks
+
+        rb = synthetic_ref_blocks(cfg, 1, seed=5, device=dev)
+        for _ in range(args.warmup):
+            ref_forward(cfg, rb, x0[:L3], f3, 1, L3)
+        torch.cuda.synchronize()
+        s3.record()
+        for _ in range(args.steps):
+            yr = ref_forward(cfg, rb, x0[:L3], f3, 1, L3)
+        e3.record()
+        torch.cuda.synchronize()
+        ref_contract_ms = s3.elapsed_time(e3) / args.steps
+        ref_contract_finite = bool(torch.isfinite(yr.float()).all())
+        del rb, yr
 
     # ------------------------------------------------------------ CPU baseline
     cpu = None
@@ -720,6 +737,10 @@ def main():
                        l2="inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"),
             "forward_ms_4050": fwd4050,
             "dit_forward_ms_4050": dit_ms,
+            "forward_ms_4050_reference_contract": ref_contract_ms,
+            "reference_contract_note": "the 28 blocks at config 3 in the reference's own contract (ConvRot 256, "
+                                       "per-row / per-channel fp32 scales, attention gate, joint kernels on e4m3 "
+                                       "code bytes; k2b.ref_blocks); output finite: " + str(ref_contract_finite),
             "dit_forward_note": "whole DiT forward at config 3 (98 text + 76x52 image tokens, 1 latent): "
                                 "patch embed, timestep MLP, 4 W4A4 text-fusion blocks (H20/KV20), 28 blocks, "
                                 "final norm + projection (k2b.dit); output finite: " + str(dit_finite),
