@@ -40,14 +40,33 @@ bool ref_group_ok(int group, int64_t k) {
 }
 // Reference-contract quantisation launch: per-row scale, optional norm +
 // modulation (x bf16 [rows, K]).
+// INT4 rows of K % 512 == 0 with a ConvRot group take the fast kernel
+// (ref_quant4_fast_kernel; bytes: e4m3 code bytes [rows, K] instead of
+// packed nibbles), the rest the one-CTA-per-row kernel.
 template <bool NORM, int BITS>
 int ref_quant_launch(const void* x, const void* w, const void* scale, const void* shift, void* q, void* s,
                      int64_t rows, int64_t K, int length, int cut, int batch, float eps, int group,
-                     cudaStream_t st) {
+                     cudaStream_t st, bool bytes = false) {
   if (rows <= 0 || K <= 0 || K % 8 || K > 32768 || rows > INT32_MAX || !ref_group_ok(group, K) || !x || !q || !s)
     return (int)cudaErrorInvalidValue;
   if (NORM && (!w || length <= 0 || batch <= 0 || (scale == nullptr) != (shift == nullptr)))
     return (int)cudaErrorInvalidValue;
+  const bool fast = BITS == 4 && K % 512 == 0 && group != 0 && aligned16(x) && aligned16(q) &&
+                    (!NORM || (aligned16(w) && (!scale || (aligned16(scale) && aligned16(shift)))));
+  if (bytes && !fast) return (int)cudaErrorInvalidValue;
+  if (fast) {
+    const size_t smem = (size_t)K * 2;
+    auto kern = bytes ? k2b::ref_quant4_fast_kernel<NORM, true> : k2b::ref_quant4_fast_kernel<NORM, false>;
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return (int)e;
+    }
+    kern<<<(unsigned)rows, k2b::kRefFastThreads, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(w), static_cast<const __nv_bfloat16*>(scale),
+        static_cast<const __nv_bfloat16*>(shift), static_cast<uint8_t*>(q), static_cast<float*>(s), (int)K, length,
+        cut, batch, eps, group);
+    return (int)cudaGetLastError();
+  }
   const size_t smem = (size_t)K * 2;
   auto kern = k2b::ref_quant_kernel<NORM, BITS>;
   if (smem > 48 * 1024) {
@@ -95,6 +114,22 @@ K2B_EXPORT void k2_quant4(const void* x, void* q, void* s, int64_t m, int64_t k,
                   ? (int)cudaErrorInvalidValue
                   : ref_quant_launch<false, 4>(x, nullptr, nullptr, nullptr, q, s, m, k, 1, -1, 1, 0.0f, group,
                                                (cudaStream_t)stream));
+}
+
+// k2_quant4 / k2_norm_mod_quant4 with the codes as e4m3 bytes [rows, K] (the
+// byte-operand GEMMs' container) instead of packed nibbles; K % 512 == 0.
+K2B_EXPORT int k2b_ref_quant4_e4m3(const void* x, void* q8, void* s, long long m, long long k, int group,
+                                   void* stream) {
+  if (group == 0) return (int)cudaErrorInvalidValue;
+  return ref_quant_launch<false, 4>(x, nullptr, nullptr, nullptr, q8, s, m, k, 1, -1, 1, 0.0f, group,
+                                    (cudaStream_t)stream, true);
+}
+K2B_EXPORT int k2b_ref_norm_quant4_e4m3(const void* x, const void* norm, const void* scale, const void* shift,
+                                        void* q8, void* scales, int rows, int K, int length, int cut, int batch,
+                                        float eps, int group, void* stream) {
+  if (group == 0 || !scale || !shift) return (int)cudaErrorInvalidValue;
+  return ref_quant_launch<true, 4>(x, norm, scale, shift, q8, scales, rows, K, length, cut, batch, eps, group,
+                                   (cudaStream_t)stream, true);
 }
 
 // kernels/native_dispatch.cu:30-33: rowwise int8 (after ConvRot when group

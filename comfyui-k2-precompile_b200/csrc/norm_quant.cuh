@@ -72,7 +72,9 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
   __shared__ float s_inv[kNqRows];
   __shared__ int s_lat[kNqRows];  // modulation row (latent) of each tile row
   __shared__ __align__(16) float s_tr[4][4 * kNqGroupFloats];
-  __shared__ __align__(16) uint8_t s_codes[4][320];
+  // code staging per warp: packed nibbles (64 bytes per group, groups
+  // 16 bytes apart in pairs) or, BYTES, e4m3 bytes (128 per group at 144 g)
+  __shared__ __align__(16) uint8_t s_codes[4][BYTES ? 4 * 144 : 320];
   __shared__ float s_rcp[1024];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 3, v = lane & 7;  // group within the slab, lane within the group
@@ -246,25 +248,42 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
           const float c = quant_c_table(qg.sd, s_rcp);
           const bool clamp = __any_sync(0xffffffffu, qg.clamp);
           const float2 c2 = make_float2(c, c), mg = make_float2(kRoundMagic8, kRoundMagic8);
+          if constexpr (BYTES) {
+            // code = r - (1.5*2^23 + 8) exactly, then two codes per e4m3x2
+            // conversion (-8..7 are exact e4m3 values; the second source is
+            // the low byte), staged in column order; this lane's 16 columns
+            // then leave as one 16-byte store
+            uint8_t* cb8 = cb + 144 * g;
 #pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            float2 r2 = __ffma2_rn(o[m], c2, mg);
-            if (clamp) {
-              r2.x = fminf(fmaxf(r2.x, kRoundMagic), kRoundMagic + 15.0f);
-              r2.y = fminf(fmaxf(r2.y, kRoundMagic), kRoundMagic + 15.0f);
+            for (int m = 0; m < 8; ++m) {
+              float2 r2 = __ffma2_rn(o[m], c2, mg);
+              if (clamp) {
+                r2.x = fminf(fmaxf(r2.x, kRoundMagic), kRoundMagic + 15.0f);
+                r2.y = fminf(fmaxf(r2.y, kRoundMagic), kRoundMagic + 15.0f);
+              }
+              const float2 cf = __fadd2_rn(r2, make_float2(-kRoundMagic8, -kRoundMagic8));
+              uint16_t e;
+              asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(e) : "f"(cf.y), "f"(cf.x));
+              *reinterpret_cast<uint16_t*>(cb8 + 2 * v + 16 * m) = e;
             }
-            // low byte = offset-8 nibbles (even element low); bits 4..21 of
-            // each word are zero, so the shifted add carries nothing into it
-            cb[cpos + v + 8 * m] = (uint8_t)((__float_as_uint(r2.y) << 4) + __float_as_uint(r2.x));
-          }
-          __syncwarp();
-          uint2 packed = *reinterpret_cast<const uint2*>(cb + cpos + 8 * v);
-          packed.x ^= 0x88888888u;  // offset-8 -> two's-complement nibbles
-          packed.y ^= 0x88888888u;
-          if constexpr (BYTES) {  // this lane's 16 columns as e4m3 bytes
-            *reinterpret_cast<uint4*>(qp) = make_uint4(e4m3x4_from_s4x4(packed.x), e4m3x4_from_s4x4(packed.x >> 16),
-                                                       e4m3x4_from_s4x4(packed.y), e4m3x4_from_s4x4(packed.y >> 16));
+            __syncwarp();
+            *reinterpret_cast<uint4*>(qp) = *reinterpret_cast<const uint4*>(cb8 + 16 * v);
           } else {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+              float2 r2 = __ffma2_rn(o[m], c2, mg);
+              if (clamp) {
+                r2.x = fminf(fmaxf(r2.x, kRoundMagic), kRoundMagic + 15.0f);
+                r2.y = fminf(fmaxf(r2.y, kRoundMagic), kRoundMagic + 15.0f);
+              }
+              // low byte = offset-8 nibbles (even element low); bits 4..21 of
+              // each word are zero, so the shifted add carries nothing into it
+              cb[cpos + v + 8 * m] = (uint8_t)((__float_as_uint(r2.y) << 4) + __float_as_uint(r2.x));
+            }
+            __syncwarp();
+            uint2 packed = *reinterpret_cast<const uint2*>(cb + cpos + 8 * v);
+            packed.x ^= 0x88888888u;  // offset-8 -> two's-complement nibbles
+            packed.y ^= 0x88888888u;
             *reinterpret_cast<uint2*>(qp) = packed;
           }
           if (v == 0) *sp = qg.scale;

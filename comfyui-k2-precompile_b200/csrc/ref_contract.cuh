@@ -146,6 +146,195 @@ __global__ void __launch_bounds__(kRefThreads) ref_quant_kernel(const __nv_bfloa
   }
 }
 
+// The INT4 quantiser above for rows of K % 512 == 0 and a ConvRot group of
+// 16, 64 or 256 (the reference checkpoints' case), with the same arithmetic
+// and rounding points, laid out for throughput: one CTA of 4 warps per row.
+// * NORM: thread t (= reference lane t of the 128) runs its fmaf chain over
+//   columns 512 i + 4 t .. +3, then the reference's shfl_down tree and
+//   (s2 + s0) + (s3 + s1) (kernels/norm_quant.cu:20-31);
+// * warp w takes the 512-column slabs w, w + 4, ...: lane l loads columns
+//   16 l .. +15 (two 16-byte loads), normalises / modulates them, and runs the
+//   stride-1 and stride-4 radix-4 stages in registers; for groups of 64 and
+//   256 a 1 KB shared transpose gives half-warp h of the slab's 256-column
+//   block h, lane r holding columns r + 16 j, j = 0..15, where the stride-16
+//   and stride-64 stages are in registers too;
+// * the rotated row (bf16, K*2 bytes of shared memory) and a block max give
+//   the row scale; thread t then quantises 16 consecutive columns at a time
+//   and stores them with one 8-byte (packed) or 16-byte (BYTES: e4m3 code
+//   bytes [rows, K], the byte-operand GEMMs' container) store.
+constexpr int kRefFastThreads = 128;
+
+__device__ __forceinline__ void ref_quad(float& a, float& b, float& c, float& d) {
+  const float s01 = __fadd_rn(a, b), d01 = __fsub_rn(a, b), s23 = __fadd_rn(c, d), d23 = __fsub_rn(c, d);
+  a = bf16_round(__fmul_rn(__fadd_rn(s01, s23), 0.5f));
+  b = bf16_round(__fmul_rn(__fadd_rn(d01, d23), 0.5f));
+  c = bf16_round(__fmul_rn(__fsub_rn(s01, s23), 0.5f));
+  d = bf16_round(__fmul_rn(__fsub_rn(d01, d23), 0.5f));
+}
+
+template <bool NORM, bool BYTES>
+__global__ void __launch_bounds__(kRefFastThreads) ref_quant4_fast_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, const __nv_bfloat16* __restrict__ scale,
+    const __nv_bfloat16* __restrict__ shift, uint8_t* __restrict__ q, float* __restrict__ s, int K, int length,
+    int cut, int batch, float eps, int group) {
+  extern __shared__ __align__(16) uint8_t ref_fast_smem[];
+  __nv_bfloat16* v = reinterpret_cast<__nv_bfloat16*>(ref_fast_smem);  // rotated row [K]
+  __shared__ __align__(16) __nv_bfloat16 tr[4][512];
+  __shared__ float red[8];
+  const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const __nv_bfloat16* xr = x + (int64_t)row * K;
+  float inv = 0.0f;
+  int bb = 0;
+  if (NORM) {
+    float sum = 0.0f;
+    for (int col = 4 * tid; col < K; col += 512) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(xr + col));
+      const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      sum = __fmaf_rn(p0.x, p0.x, sum);
+      sum = __fmaf_rn(p0.y, p0.y, sum);
+      sum = __fmaf_rn(p1.x, p1.x, sum);
+      sum = __fmaf_rn(p1.y, p1.y, sum);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) sum = __fadd_rn(sum, __shfl_down_sync(0xffffffffu, sum, off));
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    const float total = __fadd_rn(__fadd_rn(red[2], red[0]), __fadd_rn(red[3], red[1]));
+    inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), eps));
+    bb = row / length;
+    if (cut >= 0 && row % length >= cut) bb += batch;
+  }
+  float amax = 0.0f;
+  const int h = lane >> 4, r = lane & 15;
+  for (int slab = warp; slab < (K >> 9); slab += 4) {
+    const int col = 512 * slab + 16 * lane;
+    float e[16];
+    {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(xr + col));
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(xr + col + 8));
+      const uint32_t ws[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[k]));
+        e[2 * k] = f.x;
+        e[2 * k + 1] = f.y;
+      }
+    }
+    if (NORM) {
+#pragma unroll
+      for (int k = 0; k < 16; k += 4) {
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w + col + k));
+        const float wk[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) e[k + j] = bf16_round(__fmul_rn(__fmul_rn(e[k + j], inv), __fadd_rn(wk[j], 1.0f)));
+      }
+      if (scale) {
+        const __nv_bfloat16* sc = scale + (int64_t)bb * K + col;
+        const __nv_bfloat16* sh = shift + (int64_t)bb * K + col;
+#pragma unroll
+        for (int k = 0; k < 16; k += 8) {
+          const uint4 su = __ldg(reinterpret_cast<const uint4*>(sc + k));
+          const uint4 hu = __ldg(reinterpret_cast<const uint4*>(sh + k));
+          const uint32_t sw[4] = {su.x, su.y, su.z, su.w}, hw[4] = {hu.x, hu.y, hu.z, hu.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 sf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sw[j]));
+            const float2 hf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hw[j]));
+            float& y0 = e[k + 2 * j];
+            float& y1 = e[k + 2 * j + 1];
+            y0 = bf16_round(__fadd_rn(bf16_round(__fmul_rn(y0, bf16_round(__fadd_rn(sf.x, 1.0f)))), hf.x));
+            y1 = bf16_round(__fadd_rn(bf16_round(__fmul_rn(y1, bf16_round(__fadd_rn(sf.y, 1.0f)))), hf.y));
+          }
+        }
+      }
+    }
+    // stride 1 and stride 4 (16 consecutive columns per lane)
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) ref_quad(e[k], e[k + 1], e[k + 2], e[k + 3]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ref_quad(e[k], e[k + 4], e[k + 8], e[k + 12]);
+    if (group == 16) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const __nv_bfloat162 t2 = __floats2bfloat162_rn(e[2 * k], e[2 * k + 1]);
+        pk[k] = *reinterpret_cast<const uint32_t*>(&t2);
+        amax = fmax3(amax, fabsf(e[2 * k]), fabsf(e[2 * k + 1]));
+      }
+      *reinterpret_cast<uint4*>(v + col) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(v + col + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      continue;
+    }
+    // to the strided layout: half-warp h holds the slab's 256-column block h,
+    // lane r the columns r + 16 j
+    {
+      uint32_t pk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const __nv_bfloat162 t2 = __floats2bfloat162_rn(e[2 * k], e[2 * k + 1]);
+        pk[k] = *reinterpret_cast<const uint32_t*>(&t2);
+      }
+      __syncwarp();
+      *reinterpret_cast<uint4*>(&tr[warp][16 * lane]) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(&tr[warp][16 * lane + 8]) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) e[j] = __bfloat162float(tr[warp][256 * h + r + 16 * j]);
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) ref_quad(e[k], e[k + 1], e[k + 2], e[k + 3]);  // stride 16
+    if (group == 256) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) ref_quad(e[k], e[k + 4], e[k + 8], e[k + 12]);  // stride 64
+    }
+    __nv_bfloat16* vb = v + 512 * slab + 256 * h + r;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      vb[16 * j] = __float2bfloat16_rn(e[j]);
+      amax = fmaxf(amax, fabsf(e[j]));
+    }
+  }
+  // row scale: block max (NaN ignored by fmaxf, infinity clamped)
+#pragma unroll
+  for (int d = 16; d; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+  if (NORM) __syncthreads();  // red[] reuse after the sum of squares
+  if (lane == 0) red[4 + warp] = amax;
+  __syncthreads();
+  const float m = fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7]));
+  const float sc = fmaxf(__fdiv_rn(fminf(m, kBf16MaxFinite), 7.0f), 1e-10f);
+  if (tid == 0) s[row] = sc;
+  const float inverse = __fdiv_rn(1.0f, sc);
+  for (int c = 16 * tid; c < K; c += 16 * kRefFastThreads) {
+    const uint4 a = *reinterpret_cast<const uint4*>(v + c);
+    const uint4 b = *reinterpret_cast<const uint4*>(v + c + 8);
+    const uint32_t ws[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float cd[16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[k]));
+      cd[2 * k] = fminf(fmaxf(rintf(__fmul_rn(f.x, inverse)), -8.0f), 7.0f);
+      cd[2 * k + 1] = fminf(fmaxf(rintf(__fmul_rn(f.y, inverse)), -8.0f), 7.0f);
+    }
+    if (BYTES) {
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint16_t lo, hi;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(cd[4 * k + 1]), "f"(cd[4 * k]));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(cd[4 * k + 3]), "f"(cd[4 * k + 2]));
+        o[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+      }
+      *reinterpret_cast<uint4*>(q + (int64_t)row * K + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      uint32_t o[2] = {0u, 0u};
+#pragma unroll
+      for (int k = 0; k < 16; ++k) o[k >> 3] |= ((uint32_t)(int)cd[k] & 0xFu) << (4 * (k & 7));
+      *reinterpret_cast<uint2*>(q + (int64_t)row * (K / 2) + c / 2) = make_uint2(o[0], o[1]);
+    }
+  }
+}
+
 // k2_dequant8 of the reference contract: out = bf16(fp32(fp32(float(a) *
 // xs[r]) * ws[c or 0]) + bias[c]) for int32 a [m, n]; ns = 1 (one weight
 // scale) or n (per channel); bias bf16 [n] or null.

@@ -67,6 +67,8 @@ SIGNATURES = {
     "k2b_ref_qkv": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
     "k2b_ref_gated_residual": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
     "k2b_ref_qkv8": (_I, [_P] * 17 + [_I, _I, _I, _I, _I, _F, _F, _P]),
+    "k2b_ref_quant4_e4m3": (_I, [_P, _P, _P, ctypes.c_longlong, ctypes.c_longlong, _I, _P]),
+    "k2b_ref_norm_quant4_e4m3": (_I, [_P] * 6 + [_I, _I, _I, _I, _I, _F, _I, _P]),
     "k2b_ref_swiglu8": (_I, [_P] * 7 + [_I, _I, _I, _P]),
     "k2b_ref_gated_residual8": (_I, [_P] * 7 + [_I, _I, _I, _I, _P]),
     "k2_gemm4": (None, [_P] * 6 + [ctypes.c_int64] * 3 + [_I, _P]),

@@ -359,11 +359,25 @@ def _freqs_for(freqs: torch.Tensor, length: int) -> torch.Tensor:
 # ----------------------------------------- reference contract (Binding.ref)
 
 
+def _ref_q4(x2: torch.Tensor, group: int):
+    """Per-row INT4 after ConvRot (k2_quant4's arithmetic), the codes as e4m3
+    bytes when the width allows (the byte-operand GEMMs' container), else
+    packed."""
+    if x2.shape[1] % 512 == 0:
+        return ref_ops.quant4_e4m3(x2, group)
+    return ref_ops.quant4(x2, group)
+
+
+def _codes(a: torch.Tensor) -> torch.Tensor:
+    """INT4 codes as e4m3 bytes, expanding packed ones."""
+    return a if a.dtype == torch.float8_e4m3fn else ref_ops.codes_e4m3(a)
+
+
 def _ref_quantize(x2: torch.Tensor, r: RefWeight):
     """native_runtime.cpp:266-285: per-row INT4 / INT8 after ConvRot, or FP8
     with one scale (the binding's input scale, else amax / fmax)."""
     if r.format == 1:
-        return ref_ops.quant4(x2, r.group)
+        return _ref_q4(x2, r.group)
     if r.format == 2:
         return ref_ops.quant8(x2, r.group)
     scale = r.input_scale if r.input_scale is not None else ref_ops.fp8_scale(x2, r.format)
@@ -383,10 +397,12 @@ def _ref_project(x2: torch.Tensor, r: RefWeight, q=None) -> torch.Tensor:
     if r.format == 0:
         return torch.nn.functional.linear(x2, r.w, r.bias)
     qa, qs = _ref_quantize(x2, r) if q is None else q
-    qa = _pad_k(qa, r)
     if r.format == 1:
-        out = ref_ops.gemm_f8(ref_ops.codes_e4m3(qa), qs.reshape(-1), r.codes8(), r.ws, r.bias)
-    elif r.format == 2:
+        a8 = qa if qa.dtype == torch.float8_e4m3fn else ref_ops.codes_e4m3(_pad_k(qa, r))
+        out = ref_ops.gemm_f8(a8, qs.reshape(-1), r.codes8(), r.ws, r.bias)
+        return out[:, :r.n] if out.shape[1] != r.n else out
+    qa = _pad_k(qa, r)
+    if r.format == 2:
         out = ref_ops.gemm8(qa, qs.reshape(-1), r.w, r.ws, r.bias)
     else:
         out = ref_ops.gemm_f8(qa, qs.reshape(-1), r.w, r.ws, r.bias)
@@ -419,9 +435,9 @@ def _linear(x: torch.Tensor, key: int, gate: Optional[torch.Tensor] = None,
         g = gate.reshape(-1, r.n).contiguous()
         if g.shape[0] == 1 and rows // length > 1:
             g = g.expand(rows // length, r.n).contiguous()
-        qa, qs = ref_ops.quant4(x2, r.group)
+        qa, qs = _ref_q4(x2, r.group)
         b.count("gated_gemm")
-        out = ref_ops.gated_residual8(ref_ops.codes_e4m3(qa), qs.reshape(-1), r.codes8(), r.ws, g,
+        out = ref_ops.gated_residual8(_codes(qa), qs.reshape(-1), r.codes8(), r.ws, g,
                                       residual.reshape(rows, r.n).contiguous(), length=length)
         return out.reshape(residual.shape)
     out = _ref_project(x2, r).reshape(shape)
@@ -544,7 +560,7 @@ def _ref_qkv(x, qa, qs, freqs, keys, norms, heads, kvheads, sigmoid_gate=True):
     B, L = int(x.shape[0]), int(x.shape[1])
     bs = [_proj(k) for k in keys]
     nq, nk = _norm(norms[0]), _norm(norms[1])
-    a8 = ref_ops.codes_e4m3(qa)
+    a8 = _codes(qa)
     ws = [b.ref.ws for b in bs]
     q, k, v, g = ref_ops.qkv8(a8, qs.reshape(-1), [b.ref.codes8() for b in bs[:4 if sigmoid_gate else 3]],
                               ws[:4 if sigmoid_gate else 3], nq.tensors[0], nk.tensors[0], _freqs_for(freqs, L),
@@ -658,7 +674,7 @@ def _joint_qkv(x, freqs, keys, norms, heads, kvheads):
         bs[0].count("joint_qkv")
         return _b128_qkv(x, a, s, freqs, keys, heads, kvheads, norms)
     if _all_int4(bs):
-        a, s = ref_ops.quant4(x.reshape(rows, K).contiguous(), bs[0].group)
+        a, s = _ref_q4(x.reshape(rows, K).contiguous(), bs[0].group)
         bs[0].count("joint_qkv")
         return _ref_qkv(x, a, s, freqs, keys, norms, heads, kvheads)
     bs[0].count("routed_qkv_split")
@@ -690,7 +706,7 @@ def _swiglu_common(x, a, s, keys, width):
     if wg.weight is not None and wu.weight is not None:
         return ops.swiglu_bf16(a, s, wg.weight, wu.weight).reshape(shape)
     if _all_int4([wg, wu]):
-        return ref_ops.swiglu8(ref_ops.codes_e4m3(a), s.reshape(-1), wg.ref.codes8(), wg.ref.ws, wu.ref.codes8(),
+        return ref_ops.swiglu8(_codes(a), s.reshape(-1), wg.ref.codes8(), wg.ref.ws, wu.ref.codes8(),
                                wu.ref.ws).reshape(shape)
     raise RuntimeError("Joint SwiGLU weight contract changed")
 
@@ -714,7 +730,7 @@ def _joint_swiglu(x, keys, width):
     if all(b.weight is not None for b in bs):
         a, s = ops.rotate_quant(x2)
     elif _all_int4(bs):
-        a, s = ref_ops.quant4(x2, bs[0].group)
+        a, s = _ref_q4(x2, bs[0].group)
     else:
         bs[0].count("routed_swiglu_split")
         pg, pu = _group(x, keys)
@@ -748,7 +764,7 @@ def _attention_inputs(x, freqs, keys, widths, norms, heads, kvheads):
         return _b128_qkv(x, a, s, freqs, keys, heads, kvheads, norms, sigmoid_gate=False)
     if freqs is not None and _all_int4(bs):
         rows, _, K = _rows_len(x)
-        a, s = ref_ops.quant4(x.reshape(rows, K).contiguous(), bs[0].group)
+        a, s = _ref_q4(x.reshape(rows, K).contiguous(), bs[0].group)
         return _ref_qkv(x, a, s, freqs, keys, norms, heads, kvheads, sigmoid_gate=False)
     return _split_qkv(x, keys, norms, freqs, heads, kvheads, sigmoid_gate=False)
 

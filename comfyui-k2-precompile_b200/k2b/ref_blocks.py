@@ -5,7 +5,7 @@ The per-block dataflow is graph_model.block's input-quant chain
 (graph_model.py:108-114) as the reference's runtime serves it
 (native_runtime.cpp:262-311, 399-475):
 
-    q, s   = norm_quant4(x; ps, ph)               ConvRot group, one fp32 scale per row
+    q, s   = norm_quant4(x; ps, ph)               ConvRot group, one fp32 scale per row (codes as e4m3 bytes)
     Q,K,V,G = joint QKV (Q/K RMSNorm + RoPE, V, sigmoid gate)   N = 6144+1536+1536+6144
     o      = GQA attention(Q, K, V) * G            (gate pre-sigmoided)
     x1     = T(x + T(T(proj_o(quant4(o))) * pg))
@@ -72,23 +72,21 @@ def ref_block(cfg: ModelConfig, b: RefBlockWeights, x: torch.Tensor, freqs: torc
     """One block of the reference contract; x bf16 [batch*length, hidden]."""
     ps, ph, pg, ss, sh, sg = b.mod.unbind(0)
     rows = batch * length
-    q, s = ref_ops.norm_quant4(x, b.prenorm, ps, ph, length=length, eps=cfg.eps, group=group)
+    q, s = ref_ops.norm_quant4_e4m3(x, b.prenorm, ps, ph, length=length, eps=cfg.eps, group=group)
     names = ("wq", "wk", "wv", "wg_attn")
-    Q, K, V, G = ref_ops.qkv8(ref_ops.codes_e4m3(q), s.reshape(-1), [b.w[n][2] for n in names],
+    Q, K, V, G = ref_ops.qkv8(q, s.reshape(-1), [b.w[n][2] for n in names],
                               [b.w[n][1] for n in names], b.qnorm, b.knorm, freqs, length=length,
                               eps_q=cfg.qk_eps, eps_k=cfg.qk_eps)
     view = lambda t, h: t.view(batch, length, h, 128).transpose(1, 2)
     o = ops.attention(view(Q, cfg.heads), view(K, cfg.kvheads), view(V, cfg.kvheads),
                       gate=G.view(batch, length, -1), gate_is_sigmoid=True)
-    qo, so = ref_ops.quant4(o.view(rows, -1), group)
-    x1 = ref_ops.gated_residual8(ref_ops.codes_e4m3(qo), so.reshape(-1), b.w["wo"][2], b.w["wo"][1],
-                                 pg.contiguous(), x, length=length)
-    q, s = ref_ops.norm_quant4(x1, b.postnorm, ss, sh, length=length, eps=cfg.eps, group=group)
-    h = ref_ops.swiglu8(ref_ops.codes_e4m3(q), s.reshape(-1), b.w["wg"][2], b.w["wg"][1], b.w["wu"][2],
-                        b.w["wu"][1])
-    qh, sh_ = ref_ops.quant4(h, group)
-    return ref_ops.gated_residual8(ref_ops.codes_e4m3(qh), sh_.reshape(-1), b.w["wd"][2], b.w["wd"][1],
-                                   sg.contiguous(), x1, length=length)
+    qo, so = ref_ops.quant4_e4m3(o.view(rows, -1), group)
+    x1 = ref_ops.gated_residual8(qo, so.reshape(-1), b.w["wo"][2], b.w["wo"][1], pg.contiguous(), x, length=length)
+    q, s = ref_ops.norm_quant4_e4m3(x1, b.postnorm, ss, sh, length=length, eps=cfg.eps, group=group)
+    h = ref_ops.swiglu8(q, s.reshape(-1), b.w["wg"][2], b.w["wg"][1], b.w["wu"][2], b.w["wu"][1])
+    qh, sh_ = ref_ops.quant4_e4m3(h, group)
+    return ref_ops.gated_residual8(qh, sh_.reshape(-1), b.w["wd"][2], b.w["wd"][1], sg.contiguous(), x1,
+                                   length=length)
 
 
 def ref_forward(cfg: ModelConfig, blocks: List[RefBlockWeights], x: torch.Tensor, freqs: torch.Tensor, batch: int,

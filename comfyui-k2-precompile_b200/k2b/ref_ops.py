@@ -273,6 +273,42 @@ def codes_e4m3(packed: torch.Tensor) -> torch.Tensor:
     return expand_e4m3(packed.view(torch.uint8)).view(torch.float8_e4m3fn)
 
 
+def quant4_e4m3(x: torch.Tensor, group: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """quant4 with the codes as e4m3 bytes: (float8_e4m3fn [m, k], fp32 [m, 1])
+    (k2b_ref_quant4_e4m3; k % 512 == 0)."""
+    _cuda(x)
+    _bf16(x, "quant4_e4m3")
+    _need(group in GROUPS4, f"quant4_e4m3: ConvRot group {group} not in {GROUPS4}")
+    m, k = x.shape
+    _need(k % 512 == 0, "quant4_e4m3: k must be a multiple of 512")
+    q = torch.empty((m, k), dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    if m:
+        check(lib().k2b_ref_quant4_e4m3(_p(x), _p(q), _p(s), m, k, group, _stream()), "k2b_ref_quant4_e4m3")
+    return q, s
+
+
+def norm_quant4_e4m3(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, *, length: int,
+                     cut: int = -1, eps: float = 1e-6, group: int = 256) -> Tuple[torch.Tensor, torch.Tensor]:
+    """norm_quant4 with the codes as e4m3 bytes (k2b_ref_norm_quant4_e4m3)."""
+    _cuda(x, w, scale, shift)
+    _bf16(x, "norm_quant4_e4m3")
+    _need(scale.dtype == torch.bfloat16 and shift.dtype == torch.bfloat16 and w.dtype == torch.float32,
+          "norm_quant4_e4m3: fp32 norm weight and bf16 modulation expected")
+    _need(group in GROUPS4, f"norm_quant4_e4m3: ConvRot group {group} not in {GROUPS4}")
+    rows, K = x.shape
+    _need(K % 512 == 0 and w.numel() == K and scale.shape[-1] == K and shift.numel() == scale.numel(),
+          "norm_quant4_e4m3: widths")
+    batch = max(1, rows // max(1, length))
+    _need(scale.numel() // K >= (2 * batch if cut >= 0 else batch), "norm_quant4_e4m3: modulation rows")
+    q = torch.empty((rows, K), dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
+    if rows:
+        check(lib().k2b_ref_norm_quant4_e4m3(_p(x), _p(w), _p(scale), _p(shift), _p(q), _p(s), rows, K, length, cut,
+                                             batch, ctypes.c_float(eps), group, _stream()), "k2b_ref_norm_quant4_e4m3")
+    return q, s
+
+
 def _codes8(a8: torch.Tensor, w8: Sequence[torch.Tensor], xs: torch.Tensor, ws: Sequence[torch.Tensor]):
     _cuda(a8, xs, *w8, *ws)
     _need(a8.dtype == torch.float8_e4m3fn and all(w.dtype == torch.float8_e4m3fn for w in w8),

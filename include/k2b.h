@@ -274,6 +274,13 @@ int k2b_ref_gated_residual(const void* a, const void* xs, const void* w, const v
  * of the packed forms.  k2b_ref_swiglu8: k2_int4_swiglu's arguments with a8,
  * wg8, wu8.  The plain projection of this form is k2b_gemm_f8 with e4m3
  * operands and per-row / per-channel scales. */
+/* k2_quant4 / k2_norm_mod_quant4 (reference contract, ConvRot group 16, 64 or
+ * 256) with the codes written as e4m3 bytes q8 [rows, K] for the forms below;
+ * K % 512 == 0. */
+int k2b_ref_quant4_e4m3(const void* x, void* q8, void* s, long long m, long long k, int group, void* stream);
+int k2b_ref_norm_quant4_e4m3(const void* x, const void* norm, const void* scale, const void* shift, void* q8,
+                             void* scales, int rows, int K, int length, int cut, int batch, float eps, int group,
+                             void* stream);
 int k2b_ref_qkv8(const void* a8, const void* xs, const void* wq, const void* sq, const void* wk, const void* sk,
                  const void* wv, const void* sv, const void* wg, const void* sg, const void* nq, const void* nk,
                  const void* freq, void* qo, void* ko, void* vo, void* go, int m, int length, int qwidth,

@@ -112,6 +112,21 @@ def test_ref_quantisers_bit_exact(cuda):
         assert rc == 0
         q_r, s_r = O.ref_quant(x, w, sc, sh, length=length, cut=cut, batch=nb, group=256)
         assert np.array_equal(q.cpu().numpy(), q_r) and np.array_equal(s.cpu().numpy()[:, 0], s_r)
+    # the e4m3 code-byte outputs hold the same codes
+    from _helpers import E4M3
+    from k2b import ref_ops
+
+    for cut in (-1, 20):
+        q8, s8 = ref_ops.norm_quant4_e4m3(t_bf16(x, cuda), t_f32(w, cuda), t_bf16(sc, cuda), t_bf16(sh, cuda),
+                                          length=length, cut=cut, group=256)
+        q_r, s_r = O.ref_quant(x, w, sc, sh, length=length, cut=cut, batch=nb, group=256)
+        assert np.array_equal(q8.view(torch.uint8).cpu().numpy(), E4M3[O.int4_codes(q_r) + 8])
+        assert np.array_equal(s8.cpu().numpy()[:, 0], s_r)
+    for group in (16, 64, 256):
+        q8, s8 = ref_ops.quant4_e4m3(t_bf16(x, cuda), group)
+        q_r, s_r = O.ref_quant(x, group=group)
+        assert np.array_equal(q8.view(torch.uint8).cpu().numpy(), E4M3[O.int4_codes(q_r) + 8])
+        assert np.array_equal(s8.cpu().numpy()[:, 0], s_r)
     # the reference contract only: group 128 and fp16 are rejected
     assert L.k2_norm_mod_quant4(_p(t_bf16(x, cuda)), _p(t_f32(w, cuda)), _p(t_bf16(sc, cuda)), _p(t_bf16(sh, cuda)),
                                 _p(q), _p(s), length * nb, K, length, -1, nb, ctypes.c_float(1e-6), 128, 2,
