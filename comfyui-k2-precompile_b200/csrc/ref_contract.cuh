@@ -313,8 +313,10 @@ __global__ void __launch_bounds__(kRefFastThreads) ref_quant4_fast_kernel(
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[k]));
-      cd[2 * k] = fminf(fmaxf(rintf(__fmul_rn(f.x, inverse)), -8.0f), 7.0f);
-      cd[2 * k + 1] = fminf(fmaxf(rintf(__fmul_rn(f.y, inverse)), -8.0f), 7.0f);
+      // + 0: a code of -0 (rint of a small negative value) becomes +0, the
+      // e4m3 container's zero byte
+      cd[2 * k] = __fadd_rn(fminf(fmaxf(rintf(__fmul_rn(f.x, inverse)), -8.0f), 7.0f), 0.0f);
+      cd[2 * k + 1] = __fadd_rn(fminf(fmaxf(rintf(__fmul_rn(f.y, inverse)), -8.0f), 7.0f), 0.0f);
     }
     if (BYTES) {
       uint32_t o[4];
