@@ -247,13 +247,6 @@ def rotate_quant(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
 
 # --------------------------------------------------------------------- GEMM
 
-def _act(a: torch.Tensor, sa: torch.Tensor, k: int) -> int:
-    _need(a.dtype == torch.uint8 and sa.dtype == torch.float16, "packed uint8 activations + fp16 scales expected")
-    _need(a.dim() == 2 and a.shape[1] * 2 == k and tuple(sa.shape) == (a.shape[0], k // GROUP),
-          "activation / weight K mismatch")
-    return int(a.shape[0])
-
-
 def expand_e4m3(a: torch.Tensor) -> torch.Tensor:
     """Packed INT4 codes uint8 [m, k/2] -> e4m3 bytes uint8 [m, k] (k2b_expand_e4m3)."""
     _cuda(a)
