@@ -60,3 +60,33 @@ def test_single_and_ragged_rows_bitexact(cuda, rows):
     out = ops.gemm_f32(q, s, W)
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), O.gemm_w4a4(qr, sr, wq, ws))
+
+
+@pytest.mark.parametrize("rows", [0, 1, 7])
+def test_reference_contract_empty_and_ragged_rows(cuda, rows):
+    """The reference contract's quantisers and byte-operand projections on
+    empty and ragged row counts: empty outputs without a launch, and single /
+    odd rows bit-exact (the last 256-row pair of the GEMM mostly empty)."""
+    import torch
+    from k2b import ref_ops
+
+    K, N = 1024, 256
+    xb = bf16_x(rows, K, 40 + rows, outliers=False)
+    x = t_bf16(xb, cuda) if rows else torch.empty((0, K), dtype=torch.bfloat16, device=cuda)
+    q8, s8 = ref_ops.quant4_e4m3(x, 64)
+    q, s = ref_ops.quant4(x, 64)
+    assert q8.shape == (rows, K) and q.shape == (rows, K // 2) and s.shape == (rows, 1)
+    rng = np.random.default_rng(41)
+    codes = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    packed = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).astype(np.uint8)
+    ws = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    Wp, WS = t_u8(packed, cuda).view(torch.int8), t_f32(ws, cuda)
+    W8 = ref_ops.codes_e4m3(Wp)
+    out = ref_ops.gemm_f8(q8, s8.reshape(-1), W8, WS)
+    assert out.shape == (rows, N)
+    torch.cuda.synchronize()
+    if rows:
+        q_r, s_r = O.ref_quant(xb, group=64)
+        assert np.array_equal(q.view(torch.uint8).cpu().numpy(), q_r)
+        assert np.array_equal(bits(out), O.bf16_bits(O.ref_project(O.int4_codes(q_r), s_r, codes, ws)))
+        assert torch.equal(out, ref_ops.gemm4(q, s.reshape(-1), Wp, WS))
