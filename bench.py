@@ -157,7 +157,7 @@ def run_reference(args, rank):
     line = {
         "metric": METRIC, "value": value, "unit": "latents/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_latent * LATENTS * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "w4a4-s8xs8->s32 / bf16 attention",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "w4a4: int4 x int4 codes -> exact fp32 group sums / bf16 attention",
         "data": "synthetic",
         "config": dict(workload_config(), parallelism=f"host CPU, {threads} threads",
                        sampling="bounded row sample per step, extrapolated (see cpu_baseline.sample)"),
@@ -731,7 +731,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "latents/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "w4a4-s8xs8->s32 / bf16 attention", "data": "synthetic",
+            "vs_baseline": None, "dtype": "w4a4: int4 x int4 codes -> exact fp32 group sums / bf16 attention", "data": "synthetic",
             "config": dict(workload_config(),
                        parallelism=par, tp=tp, dp=topo.dp, latents_per_group=local,
                        l2="inputs larger than L2 (11 GB resident weights + 415 MB hidden states per step)"),
