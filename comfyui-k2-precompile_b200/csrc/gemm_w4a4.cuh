@@ -523,8 +523,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc2[j] = make_float2(0.0f, 0.0f);
     // TMEM loads are software-pipelined: the load of chunk c+1 (16 columns)
-    // is in flight while chunk c is dequantised, and the first load of group
-    // g+1 overlaps the last chunk of group g.  Barriers, scales and the abort
+    // is in flight while chunk c is dequantised.  Barriers, scales and the abort
     // flag are addressed with 32-bit shared addresses to leave the registers
     // to the accumulators and the two load buffers.
     const uint32_t s_full_sc = smem_u32(full_sc), s_empty_sc = smem_u32(empty_sc);
@@ -616,6 +615,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       __half sa_next = sa_row[0];  // activation scales are prefetched one group ahead
       for (int g = 0; g < G && ok; ++g) {
+        if (g > 0) {
+          // group g's scales (first group of a chunk) and accumulators; every
+          // chunk of group g-1 was dequantised before this wait, which ends the
+          // MMA -> epilogue -> release chain of the next buffer (traced: doing
+          // the last chunk after the wait kept ~630 cycles per group on it)
+          const int c = g / kScGroups;
+          if (!((g % kScGroups != 0 ||
+                 mbar_wait_s(s_full_sc + 8u * (uint32_t)(c & 1), (c >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) &&
+                mbar_wait_s(s_tfull + 8u * (uint32_t)(g & 1), (g >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          tmem_ld16(tcol + (g & 1) * GEMM_BN, va);
+        }
         const int b = g & 1, cbuf = (g / kScGroups) & 1;
         const float sa = row_ok ? __half2float(sa_next) : 0.0f;
         if (g + 1 < G) sa_next = sa_row[g + 1];
@@ -638,18 +652,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (lane == 0) {
           if (leader) mbar_arrive_s(s_tempty + 8u * (uint32_t)b);
           else mbar_arrive_remote(tmem_empty_remote + 8u * (uint32_t)b);
-        }
-        if (g + 1 < G) {
-          const int g1 = g + 1;
-          const int c1 = g1 / kScGroups;
-          if ((g1 % kScGroups != 0 ||
-               mbar_wait_s(s_full_sc + 8u * (uint32_t)(c1 & 1), (c1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) &&
-              mbar_wait_s(s_tfull + 8u * (uint32_t)(g1 & 1), (g1 >> 1) & 1, s_abort, ERR_WAIT_EPILOGUE)) {
-            tc_fence_after();
-            tmem_ld16(tcol + (g1 & 1) * GEMM_BN, va);
-          } else {
-            ok = false;
-          }
         }
         dequant16(vb, scs + 4 * kCd + 64, 48, sa2);
         __syncwarp();
