@@ -44,15 +44,16 @@
 // Roles (640 threads per CTA):
 //   warp 0      TMA producers: lane 0 the A group tile (packed 128 x 64 B, or
 //               bytes 128 x 128 B 128B-swizzled) and this CTA's half of the W
-//               group tile (128 x 128 B, 128B-swizzled); lane 1 the W scales
-//               of all 256 columns, in chunks of 4 (SwiGLU) or 16 groups, two
-//               chunk buffers
+//               group tile (128 x 128 B, 128B-swizzled); packed A: lane 1 the
+//               W scales of all 256 columns, in chunks of 4 (SwiGLU) or 16
+//               groups, two chunk buffers (byte A: lane 0 of warp 3)
 //   warp 1      TMEM allocator (both CTAs, cta_group::2); leader: single-thread
 //               MMA issuer (4 x K=32 MMAs per group); peer: relays "stage
 //               ready" (W landed + A unpacked) to the leader
 //   warps 2-3   A unpackers (packed A): s4 -> e4m3 into the UMMA layout;
 //               byte A: lane 0 of warp 2 issues the A tensor copies (a second
-//               issuing thread: one thread's copies complete one at a time)
+//               issuing thread: one thread's copies complete one at a time) and
+//               lane 0 of warp 3 the W scales
 //   warps 4-19  epilogue: TMEM lane quadrant = warp % 4, column quarter
 //               = (warp-4)/4 (64 columns of one row per thread)
 // Stage barrier full_s[s] collects this CTA's W (and byte A) bytes (producer
@@ -346,6 +347,37 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   int issued_w = 0, issued_pa = 0, issued_sc = 0, issued_mma = 0;
+  // ------------------------------------------------ W-scale chunk producer
+  // Chunk c (groups kScGroups*c ..) goes to buffer c % 2 once the epilogue
+  // has released chunk c - 2.  A thread of its own: copies issued by one
+  // thread complete one after another, so the scale copies never queue with
+  // the W/A copies.  Byte A: lane 0 of warp 3, which has no other work, so
+  // every scheduler hosts one single-thread role (warp 0 the W copies, warp 1
+  // the MMAs, warp 2 the A copies).  The epilogue warps that share a scheduler
+  // with two divergent producer lanes of one warp were measured ~1100 cycles
+  // per K group behind the others, and the slowest warp releases the TMEM
+  // buffer.  Packed A: lane 1 of warp 0 (warps 2-3 unpack A).
+  auto scale_producer = [&]() {
+    const int nchunks = (G + kScGroups - 1) / kScGroups;
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
+      const int cb = chunk & 1;
+      if (chunk >= 2 && !mbar_wait(&empty_sc[cb], ((chunk >> 1) & 1) ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
+      const int g0 = chunk * kScGroups;
+      const int ng = min(kScGroups, G - g0);
+      mbar_arrive_expect_tx(&full_sc[cb], ng * (pairw ? GEMM_BN : vcols) * 4);
+      uint8_t* dst = smem + GEMM_OFF_SC + cb * GEMM_SC_BYTES;
+      for (int j = 0; j < ng; ++j) {
+        const int64_t off = (int64_t)(g0 + j) * S.n + n0;
+        if (pairw) {
+          bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 2, &full_sc[cb]);
+          bulk_load(dst + j * GEMM_BN * 4 + GEMM_BN * 2, S.wscale2 + off, GEMM_BN * 2, &full_sc[cb]);
+        } else {
+          bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, (uint32_t)vcols * 4u, &full_sc[cb]);
+        }
+      }
+      issued_sc = chunk + 1;
+    }
+  };
   if (warp < 4) {
     setmaxnreg_dec32();
     if (warp == 0) {
@@ -376,31 +408,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tma_load_2d(smem + GEMM_OFF_PA + ps * GEMM_PA_BYTES, &amap, &full_pa[ps], g * 64, m0);
           issued_pa = g + 1;
         }
-      } else if (lane == 1 && !REF) {
-        // ------------------------------------------ W-scale chunk producer
-        // Chunk c (groups kScGroups*c ..) goes to buffer c % 2 once the
-        // epilogue has released chunk c - 2.  A thread of its own: copies
-        // issued by one thread complete one after another, so the scale
-        // copies never queue with the W/A copies of lane 0.
-        const int nchunks = (G + kScGroups - 1) / kScGroups;
-        for (int chunk = 0; chunk < nchunks; ++chunk) {
-          const int cb = chunk & 1;
-          if (chunk >= 2 && !mbar_wait(&empty_sc[cb], ((chunk >> 1) & 1) ^ 1, abort_flag, ERR_WAIT_PRODUCER)) break;
-          const int g0 = chunk * kScGroups;
-          const int ng = min(kScGroups, G - g0);
-          mbar_arrive_expect_tx(&full_sc[cb], ng * (pairw ? GEMM_BN : vcols) * 4);
-          uint8_t* dst = smem + GEMM_OFF_SC + cb * GEMM_SC_BYTES;
-          for (int j = 0; j < ng; ++j) {
-            const int64_t off = (int64_t)(g0 + j) * S.n + n0;
-            if (pairw) {
-              bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, GEMM_BN * 2, &full_sc[cb]);
-              bulk_load(dst + j * GEMM_BN * 4 + GEMM_BN * 2, S.wscale2 + off, GEMM_BN * 2, &full_sc[cb]);
-            } else {
-              bulk_load(dst + j * GEMM_BN * 4, S.wscale + off, (uint32_t)vcols * 4u, &full_sc[cb]);
-            }
-          }
-          issued_sc = chunk + 1;
-        }
+      } else if (lane == 1 && !REF && !BYTEA) {
+        scale_producer();
       }
     } else if (warp == 1) {
       // ------------------------------------- MMA issuer (leader) / relay (peer)
@@ -445,6 +454,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_arrive_remote(ready0 + 8u * (uint32_t)s);
         }
       }
+    } else if (BYTEA && warp == 3) {
+      if (lane == 0 && !REF) scale_producer();
     } else if (BYTEA) {
       // --------------------------------------------- A producer (byte A)
       // A tensor copies go out from a warp of their own: copies issued by one
@@ -908,7 +919,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (BYTEA && warp == 2 && lane == 0)
       for (int g = (issued_pa > GEMM_STAGES ? issued_pa - GEMM_STAGES : 0); g < issued_pa; ++g)
         mbar_drain(&full_s[g % GEMM_STAGES], (g / GEMM_STAGES) & 1);
-    if (warp == 0 && lane == 1)
+    if (BYTEA ? (warp == 3 && lane == 0) : (warp == 0 && lane == 1))
       for (int c = (issued_sc > 2 ? issued_sc - 2 : 0); c < issued_sc; ++c)
         mbar_drain(&full_sc[c & 1], (c >> 1) & 1);
     if (warp == 1 && lane == 0 && issued_mma > 0) {
