@@ -432,10 +432,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + GEMM_OFF_UA + s * GEMM_UA_BYTES);
           const uint32_t w_base = smem_u32(smem + GEMM_OFF_W + s * GEMM_W_BYTES);
+          // one descriptor per operand and group; the K step of 32 bytes is +2 in
+          // the descriptor's 16-byte address field (shared addresses stay far below
+          // its 256 KB range, so the add never carries out of it)
+          const uint64_t ad0 = umma_desc_sw128(a_base, 16, 1024), bd0 = umma_desc_sw128(w_base, 16, 1024);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = umma_desc_sw128(a_base + 32 * k, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(w_base + 32 * k, 16, 1024);
+            const uint64_t ad = ad0 + 2u * k;
+            const uint64_t bd = bd0 + 2u * k;
             const uint32_t acc = (k > 0 || (REF && g > 0)) ? 1u : 0u;
             if (MODE == GM_REF8) mma_i8_pair(tmem + b * GEMM_BN, ad, bd, idesc, acc);
             else mma_f8_pair(tmem + b * GEMM_BN, ad, bd, idesc, acc);
