@@ -45,7 +45,7 @@
 //   warp 0      TMA producers: lane 0 the A group tile (packed 128 x 64 B, or
 //               bytes 128 x 128 B 128B-swizzled) and this CTA's half of the W
 //               group tile (128 x 128 B, 128B-swizzled); packed A: lane 1 the
-//               W scales of all 256 columns, in chunks of 4 (SwiGLU) or 16
+//               W scales of all 256 columns, in chunks of 8 (SwiGLU) or 16
 //               groups, two chunk buffers (byte A: lane 0 of warp 3)
 //   warp 1      TMEM allocator (both CTAs, cta_group::2); leader: single-thread
 //               MMA issuer (4 x K=32 MMAs per group); peer: relays "stage
@@ -98,10 +98,11 @@ constexpr int GEMM_W_BYTES = GEMM_BN / 2 * 128;   // 16 KB: this CTA's half of t
 constexpr int GEMM_UA_BYTES = GEMM_BM * 128;      // 16 KB
 constexpr int GEMM_PA_BYTES = GEMM_BM * 64;       // 8 KB
 // W scales arrive in chunks of up to 16 K groups, two chunk buffers of 16 KB,
-// copied by a producer lane of their own.  The SwiGLU kernel (two copies per
-// group: gate and up scales) takes chunks of 4 groups: measured gate/up
-// 14.40 ms with 16, 13.98 with 8, 13.61 with 4, 13.76 with 2; the other kinds
-// are within 0.5% between 8 and 16 and keep 16.
+// copied by a producer thread of their own.  The SwiGLU kernel (two copies per
+// group: gate and up scales) takes chunks of 8 groups: gate/up at 33792 rows
+// measured 11.15 ms with 8, 11.24 with 4, 11.38 with 16 and 11.35 with 2 (with
+// the epilogue's handoff order as built; an earlier epilogue preferred 4).  The
+// other kinds are within noise between 8 and 16 and keep 16.
 constexpr int GEMM_SC_MAX_GROUPS = 16;
 constexpr int GEMM_SC_BYTES = GEMM_BN * 4 * GEMM_SC_MAX_GROUPS;
 constexpr int GEMM_OFF_W = 0;
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                      const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kScGroups = PAIRW ? 4 : GEMM_SC_MAX_GROUPS;
+  constexpr int kScGroups = PAIRW ? 8 : GEMM_SC_MAX_GROUPS;
   // A arrives as bytes loaded by TMA (else packed INT4 unpacked by warps 2-3)
   constexpr bool BYTEA = MODE == GM_BYTES || MODE == GM_REF8 || MODE == GM_REFF8;
   constexpr bool REF = MODE >= GM_REF4;  // full-K accumulation, per-row / per-channel scales
