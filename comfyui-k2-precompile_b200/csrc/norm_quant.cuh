@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(kNqThreads, 4) norm_quant_kernel(const __nv_bf
       for (int r = warp; r < nrows; r += 4) {
         const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)(row0 + r) * K) + 2 * lane;
         float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
-#pragma unroll 4
+        // 12 loads in flight per lane (unroll 4: 229 us, 6: 226 us at 33792 x 6144)
+#pragma unroll 6
         for (int i = 0; i < slabs; ++i) {
           const uint4 a = __ldg(xr + 64 * i), b = __ldg(xr + 64 * i + 1);
           // chains: lane 4l+c <- words 2c, 2c+1 of (a, b), low half first.
