@@ -17,8 +17,9 @@ other half, the 28-block forward at 4050 tokens batch 1 (config 3), is
 measured on rank 0 at N=1 and reported as "forward_ms_4050".
 
 value: latents/s with inputs resident in HBM.  e2e: the same through the
-public forward with the step's hidden states copied host->device from pinned
-memory and the result copied back inside the timed region.
+public forward with every step's hidden states copied host->device from pinned
+memory and its result copied back inside the timed region (the copies of
+neighbouring steps overlap the forward on two copy streams, double-buffered).
 """
 from __future__ import annotations
 
@@ -616,19 +617,50 @@ def main():
     traffic = load_traffic().get(dom) if tp == 1 else None
 
     # ------------------------------------------------------------ end to end
-    for _ in range(args.warmup):
-        x.copy_(x_host, non_blocking=True)
-        wl.step(x)
-        out_host.copy_(x, non_blocking=True)
+    # Every step copies its hidden states host -> device from pinned memory and
+    # its result device -> host.  Two device buffers alternate: the input copy
+    # of step i+1 (one copy stream) and the result copy of step i (another,
+    # the other direction of the link) run while step i computes, so inside the
+    # timed region only the first input copy and the last result copy are not
+    # overlapped.
+    cur = torch.cuda.current_stream()
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+    xs = [x, torch.empty_like(x)]
+
+    def run_e2e(n):
+        mk = torch.cuda.Event
+        h2d_ev, comp_ev, d2h_ev = [mk(), mk()], [mk(), mk()], [mk(), mk()]
+        start = mk()
+        start.record(cur)
+        h2d_s.wait_event(start)
+        with torch.cuda.stream(h2d_s):
+            xs[0].copy_(x_host, non_blocking=True)
+        h2d_ev[0].record(h2d_s)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                nb = (i + 1) % 2
+                if i >= 1:
+                    h2d_s.wait_event(d2h_ev[nb])  # that buffer's previous result is out
+                with torch.cuda.stream(h2d_s):
+                    xs[nb].copy_(x_host, non_blocking=True)
+                h2d_ev[nb].record(h2d_s)
+            cur.wait_event(h2d_ev[b])
+            wl.step(xs[b])
+            comp_ev[b].record(cur)
+            d2h_s.wait_event(comp_ev[b])
+            with torch.cuda.stream(d2h_s):
+                out_host.copy_(xs[b], non_blocking=True)
+            d2h_ev[b].record(d2h_s)
+        cur.wait_event(d2h_ev[(n - 1) % 2])
+
+    run_e2e(args.warmup)
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record()
-    for _ in range(args.steps):
-        x.copy_(x_host, non_blocking=True)
-        wl.step(x)
-        out_host.copy_(x, non_blocking=True)
+    run_e2e(args.steps)
     e2.record()
     torch.cuda.synchronize()
     barrier()
